@@ -1,0 +1,484 @@
+"""Decode-GEMM benchmark on B200: the decode linears of a Qwen3-8B step.
+
+One step = every decode linear of one Qwen3-8B decode step (36 layers x {fused QKV
+4096->6144, o_proj 4096->4096, fused gate_up 4096->24576, down 12288->4096} + lm_head
+4096->151936; 15.1 GB of distinct bf16 weights), run once for each decode batch M in
+{1, 2, 4, 8, 16}. Weights ~ N(0, 0.02), activations ~ N(0, 1), synthetic (seeded).
+
+Metric: decode-GEMM HBM TB/s = algorithmic bytes 2*(K*N + M*K + M*N) summed over the step's
+GEMMs / device time. Every step streams 75 GB of distinct weights (5 x 15.1 GB), far more
+than the 126 MB L2, so no timed GEMM finds its weight in L2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun (N > 1) every rank runs the same step on its own GPU (replicas only: the
+single-GPU decode linears do not exchange data) and rank 0 prints the aggregate.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+LAYERS = 36
+HIDDEN = 4096
+VOCAB = 151936
+# (name, N, K) of one Qwen3-8B decoder layer's linears (32 Q + 8 KV heads x 128, MLP 12288).
+LAYER_LINEARS = [("qkv", 6144, 4096), ("o_proj", 4096, 4096), ("gate_up", 24576, 4096),
+                 ("down", 4096, 12288)]
+LM_HEAD = ("lm_head", VOCAB, HIDDEN)
+M_LIST = (1, 2, 4, 8, 16)
+METRIC = "decode-GEMM HBM TB/s (Qwen3-8B decode linears, M=1..16)"
+WORKLOAD = ("qwen3-8b decode linears: 36 layers x (QKV 4096x6144, o_proj 4096x4096, "
+            "gate_up 4096x24576, down 12288x4096) + lm_head 4096x151936, once per M in 1,2,4,8,16")
+
+
+def gemm_bytes(M, N, K):
+    return 2 * (K * N + M * K + M * N)
+
+
+def step_linears():
+    """The (name, N, K, layer) list of one decode step's linears, in execution order."""
+    out = []
+    for layer in range(LAYERS):
+        for name, N, K in LAYER_LINEARS:
+            out.append((name, N, K, layer))
+    out.append((*LM_HEAD, LAYERS))
+    return out
+
+
+def step_bytes(m_list):
+    return sum(gemm_bytes(M, N, K) for M in m_list for (_, N, K, _) in step_linears())
+
+
+# ---------------------------------------------------------------------------------------
+# clocks sampled with nvidia-smi during the timed region
+# ---------------------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except Exception:
+            pass
+        finally:
+            try:
+                os.unlink(self.path)
+            except Exception:
+                pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------
+# CPU baseline: the reference's own code path (torch.mm on bf16 CPU tensors, the call at
+# engine/kernels/decode.py:54-66 and engine/engine.py:114) on the host cores
+# ---------------------------------------------------------------------------------------
+def cpu_sample_linears():
+    """Bounded CPU sample: layer 0's four linears plus 1/36 of the lm_head rows."""
+    return [(name, N, K) for name, N, K in LAYER_LINEARS] + [("lm_head/36", VOCAB // LAYERS, HIDDEN)]
+
+
+def cpu_reference(m_list, budget_s=10.0, warmup=1):
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    from neokernel_b200 import synthetic
+    lin = cpu_sample_linears()
+    Ws = [synthetic.weight(N, K, seed=i) for i, (_, N, K) in enumerate(lin)]
+    xs = {(M, K): synthetic.activation(M, K, seed=M) for M in m_list for (_, _, K) in lin}
+    ys = {(M, N): torch.empty((M, N), dtype=torch.bfloat16) for M in m_list for (_, N, _) in lin}
+
+    def one_pass():
+        for M in m_list:
+            for (_, N, K), W in zip(lin, Ws):
+                torch.mm(xs[(M, K)], W.t(), out=ys[(M, N)])
+
+    for _ in range(warmup):
+        one_pass()
+    bytes_pass = sum(gemm_bytes(M, N, K) for M in m_list for (_, N, K) in lin)
+    passes, t0 = 0, time.perf_counter()
+    while True:
+        one_pass()
+        passes += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    tbs = bytes_pass * passes / el / 1e12
+    sample = (f"layer-0 QKV/o_proj/gate_up/down + lm_head rows 0..{VOCAB // LAYERS} "
+              f"(1/36 of the vocabulary) at M in {list(m_list)}; {passes} passes in {el:.1f} s; "
+              f"torch.mm bf16 on CPU (ATen), {threads} threads")
+    return {"value": round(tbs, 6), "unit": "TB/s", "cores": threads, "kind": "reference",
+            "sample": sample, "seconds_per_pass": el / passes,
+            "cpu": _cpu_model()}
+
+
+def _cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------------------
+# distributed plumbing (replicas only)
+# ---------------------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v, world, local):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local}")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reference_arm(args):
+    world, rank, _ = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
+    if rank != 0:
+        return 0
+    m_list = tuple(int(m) for m in args.m_list.split(","))
+    budget = max(2.0, min(20.0, 1.0 * max(args.steps, 1)))
+    warm = cpu_reference(m_list, budget_s=0.5, warmup=max(1, min(args.warmup, 3)))
+    base = cpu_reference(m_list, budget_s=budget, warmup=0)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": base["value"], "unit": "TB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": base["seconds_per_pass"] * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "m": list(m_list), "reference_path": "torch.mm (CPU, ATen)",
+                   "sample": base["sample"]},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": "TB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "warm_value": warm["value"],
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--m-list", default=",".join(str(m) for m in M_LIST))
+    ap.add_argument("--split", type=int, default=0, help="force split-K (0 = plan's choice)")
+    ap.add_argument("--kind", type=int, default=0, help="force kernel family (0 = auto)")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    import neokernel_b200 as nk
+    from neokernel_b200 import synthetic
+
+    m_list = tuple(int(m) for m in args.m_list.split(","))
+    lin = step_linears()
+
+    # --- resident weights: 36 layers x 4 distinct matrices + lm_head (15.1 GB) ------------
+    Ws = []
+    for i, (name, N, K, layer) in enumerate(lin):
+        Ws.append(synthetic.weight(N, K, seed=1000 * rank + i, device=dev))
+    # activations and outputs per (M, K) / (M, N); contents are re-used across layers
+    Ks = sorted({K for (_, _, K, _) in lin})
+    Ns = sorted({N for (_, N, _, _) in lin})
+    xs = {(M, K): synthetic.activation(M, K, seed=M * 31 + K, device=dev) for M in m_list for K in Ks}
+    ys = {(M, N): torch.empty((M, N), dtype=torch.bfloat16, device=dev) for M in m_list for N in Ns}
+    plans = {(M, N, K): nk.plan_for(M, N, K, kind=args.kind, split_k=args.split)
+             for M in m_list for (_, N, K, _) in lin}
+
+    stream = torch.cuda.Stream(device=dev)
+
+    def run_m(M):
+        for (name, N, K, layer), W in zip(lin, Ws):
+            nk.mm(xs[(M, K)], W.t(), out=ys[(M, N)], plan=plans[(M, N, K)], stream=stream)
+
+    # eager warm-up (sizes the workspace), then one graph per M
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        for M in m_list:
+            run_m(M)
+    stream.synchronize()
+    graphs = {}
+    for M in m_list:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            run_m(M)
+        graphs[M] = g
+    torch.cuda.synchronize(dev)
+
+    def step(evs=None):
+        for i, M in enumerate(m_list):
+            if evs is not None:
+                evs[i][0].record(stream)
+            graphs[M].replay()
+            if evs is not None:
+                evs[i][1].record(stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+
+    launches_per_step = len(lin) * len(m_list)
+    bytes_per_step = step_bytes(m_list)
+    per_m_events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                     for _ in m_list] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    # --- timed region -------------------------------------------------------------------
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for s in range(args.steps):
+                step(per_m_events[s])
+            end.record(stream)
+        end.synchronize()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = start.elapsed_time(end)
+    ms_max = max_over_ranks(ms, world, local)
+    clocks = clk.summary()
+    value = bytes_per_step * args.steps * world / (ms_max / 1e3) / 1e12
+    per_m = {}
+    for i, M in enumerate(m_list):
+        t = sum(per_m_events[s][i][0].elapsed_time(per_m_events[s][i][1]) for s in range(args.steps))
+        b = sum(gemm_bytes(M, N, K) for (_, N, K, _) in lin) * args.steps
+        per_m[str(M)] = {"TB/s": round(b / (t / 1e3) / 1e12, 4),
+                         "us_per_step": round(t * 1e3 / args.steps, 1),
+                         "tok_s_linears_only": round(M * args.steps / (t / 1e3), 1)}
+
+    # --- roofline pass: every launch bracketed by events on the launching stream ----------
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak_gbs = peaks.get("hbm_gbs")
+    peak_src = "measured" if peak_gbs else "fallback"
+    peak_gbs = peak_gbs or 6650.0
+    rl_steps = max(1, min(args.steps, 3))
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(rl_steps * launches_per_step)]
+    kbytes = []
+    torch.cuda.synchronize(dev)
+    with torch.cuda.stream(stream):
+        j = 0
+        for _ in range(rl_steps):
+            for M in m_list:
+                for (name, N, K, layer), W in zip(lin, Ws):
+                    ev[j][0].record(stream)
+                    nk.mm(xs[(M, K)], W.t(), out=ys[(M, N)], plan=plans[(M, N, K)], stream=stream)
+                    ev[j][1].record(stream)
+                    kbytes.append(gemm_bytes(M, N, K))
+                    j += 1
+    torch.cuda.synchronize(dev)
+    kt = [a.elapsed_time(b) for a, b in ev]
+    avg_ms = sum(kt) / len(kt)
+    avg_bytes = sum(kbytes) / len(kbytes)
+    achieved_gbs = avg_bytes / (avg_ms / 1e3) / 1e9
+    by_kind = {}
+    for (M, N, K), p in plans.items():
+        by_kind.setdefault(p.kind, 0)
+        by_kind[p.kind] += 1
+    roofline = {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak_gbs,
+                "unit": "GB/s", "frac": round(achieved_gbs / peak_gbs, 4),
+                "traffic": _traffic_per_launch(avg_bytes), "peak_source": f"{peak_src} hbm_gbs",
+                "kernel": "nk gemv (gemv_kernel<MT,R,U>)",
+                "launches_timed": len(kt), "avg_launch_us": round(avg_ms * 1e3, 2),
+                "algorithmic_bytes_per_launch": int(avg_bytes)}
+
+    # --- e2e through the public API with host buffers -------------------------------------
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_pass(nk, lin, Ws, m_list, plans, dev, stream, args, world, local)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_reference(m_list, budget_s=args.cpu_budget)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+            "config": {"workload": WORKLOAD, "m": list(m_list), "gemms_per_step": launches_per_step,
+                       "algorithmic_bytes_per_step": bytes_per_step,
+                       "l2": "inputs larger than L2: 15.1 GB of distinct weights per M pass",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "timing": "CUDA graph replay per M, CUDA events on the launching stream",
+                       "split_k": args.split or "plan", "kind": args.kind or "auto",
+                       "plan_kinds": {str(k): v for k, v in by_kind.items()}},
+            "per_m": per_m,
+            "roofline": roofline,
+            "cpu_baseline": ({k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+                             if cpu else None),
+            "e2e": e2e,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    for g in graphs.values():
+        del g
+    graphs.clear()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def _traffic_per_launch(avg_bytes):
+    """DRAM bytes per launch from the committed ncu capture (profiles/traffic.txt), scaled to
+    this run's average algorithmic bytes per launch; None when no capture is recorded."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    try:
+        for line in open(path):
+            if line.startswith("dram_over_algorithmic"):
+                return int(float(line.split()[1]) * avg_bytes)
+    except Exception:
+        pass
+    return None
+
+
+def e2e_pass(nk, lin, Ws, m_list, plans, dev, stream, args, world, local):
+    """Same step through ``neokernel_b200.mm`` (eager), with each step's activations copied
+    from pinned host memory to the device first and every result copied back after."""
+    x_specs = [(M, K) for M in m_list for (_, N, K, _) in lin]
+    y_specs = [(M, N) for M in m_list for (_, N, K, _) in lin]
+    x_elems = sum(M * K for M, K in x_specs)
+    y_elems = sum(M * N for M, N in y_specs)
+    hx = torch.empty(x_elems, dtype=torch.bfloat16, pin_memory=True)
+    hx.copy_(torch.randn(x_elems, dtype=torch.float32).to(torch.bfloat16))
+    hy = torch.empty(y_elems, dtype=torch.bfloat16, pin_memory=True)
+    dx = torch.empty(x_elems, dtype=torch.bfloat16, device=dev)
+    dy = torch.empty(y_elems, dtype=torch.bfloat16, device=dev)
+    xv, off = [], 0
+    for M, K in x_specs:
+        xv.append(dx[off:off + M * K].view(M, K))
+        off += M * K
+    yv, off = [], 0
+    for M, N in y_specs:
+        yv.append(dy[off:off + M * N].view(M, N))
+        off += M * N
+    calls = []
+    i = 0
+    for M in m_list:
+        for (name, N, K, layer), W in zip(lin, Ws):
+            calls.append((xv[i], W.t(), yv[i], plans[(M, N, K)]))
+            i += 1
+
+    def one():
+        dx.copy_(hx, non_blocking=True)
+        for x, wt, y, p in calls:
+            nk.mm(x, wt, out=y, plan=p, stream=stream)
+        hy.copy_(dy, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, min(args.warmup, 3))):
+            one()
+    stream.synchronize()
+    steps = max(1, min(args.steps, 5))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        for _ in range(steps):
+            one()
+        b.record(stream)
+    b.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b), world, local)
+    return {"value": round(step_bytes(m_list) * steps * world / (ms / 1e3) / 1e12, 4),
+            "unit": "TB/s", "h2d_bytes_per_step": 2 * x_elems, "d2h_bytes_per_step": 2 * y_elems,
+            "steps": steps, "ms_per_step": round(ms / steps, 3),
+            "path": "neokernel_b200.mm eager, pinned host buffers, cudaMemcpyAsync both ways"}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

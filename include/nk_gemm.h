@@ -1,0 +1,131 @@
+/*
+ * nk_gemm.h — C ABI of the B200 (sm_100a) decode-GEMM library `libnkgemm.so`.
+ *
+ * One operation is exported: the bf16 decode linear
+ *
+ *     y[M, N] = bf16_rne( sum_k  f32(x[M, k]) * f32(W[N, k]) )      (fp32 accumulation)
+ *
+ * with W a row-major [N, K] weight whose rows are K-contiguous. This is exactly the call the
+ * reference engine makes at every decode linear:
+ *
+ *     torch.mm(x, W.t(), out=y)
+ *       engine/kernels/decode.py:54   (QKV:     norm     · Wqkvᵀ,    W = cat(q, k, v))
+ *       engine/kernels/decode.py:58   (o_proj:  attn_flat · Woᵀ)
+ *       engine/kernels/decode.py:64   (gate_up: norm     · [Wg; Wu]ᵀ)
+ *       engine/kernels/decode.py:66   (down:    product  · Wdᵀ)
+ *       engine/engine.py:114          (lm_head: norm     · Eᵀ)
+ *
+ * where `W.t()` is the transposed view built in engine/kernels/weights.py:12-13,24-25 and
+ * engine/engine.py:70. The library reads that same storage: `w` below is the data pointer
+ * of the row-major [N, K] weight (the storage behind the `.t()` view), `ldw` its row stride.
+ *
+ * Conventions
+ *   - Every pointer is a CUDA device pointer except `plan` (host). No function allocates
+ *     device memory, synchronizes the host, or touches any stream other than `stream`.
+ *   - Functions return 0 (NK_OK) or a negative NK_ERR_* code and launch nothing on error.
+ *   - `stream` is a cudaStream_t (0 = legacy default stream).
+ *   - Launches are capture-safe: a sequence of nk_gemm_bf16 calls may be recorded into a
+ *     CUDA graph and replayed, provided the workspace stays the one passed at capture.
+ *   - Calls that share a workspace must be ordered (same stream, or joined by events): the
+ *     split-K tickets in the workspace belong to one call at a time.
+ */
+#ifndef NK_GEMM_H
+#define NK_GEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define NK_API __attribute__((visibility("default")))
+#else
+#define NK_API
+#endif
+
+typedef struct CUstream_st* nk_stream_t; /* identical to cudaStream_t */
+
+/* Status codes. */
+#define NK_OK              0
+#define NK_ERR_SHAPE      -1  /* M, N or K out of range, or M > plan->M_max            */
+#define NK_ERR_ALIGN      -2  /* pointer or leading dimension violates the plan's layout  */
+#define NK_ERR_WORKSPACE  -3  /* workspace missing or smaller than nk_ws_bytes(plan)     */
+#define NK_ERR_SPLIT      -4  /* split_k outside [1, 16] or larger than K allows          */
+#define NK_ERR_PLAN       -5  /* plan is NULL, corrupt, or made for another (N, K)        */
+#define NK_ERR_CUDA       -6  /* a CUDA runtime call failed (launch, attribute, symbol)   */
+#define NK_ERR_DEVICE     -7  /* current device is not sm_100 (B200 class)                */
+#define NK_ERR_TIMEOUT    -8  /* a kernel's bounded wait expired (read by nk_device_error) */
+#define NK_ERR_ARG        -9  /* any other invalid argument                               */
+
+/* Kernel families a plan can select. */
+#define NK_KIND_AUTO     0
+#define NK_KIND_GEMV     1  /* CUDA-core weight-streaming GEMV, 128-bit loads, M <= 16        */
+#define NK_KIND_TC       2  /* tcgen05/TMEM swap-AB tensor-core GEMM with a TMA smem ring     */
+#define NK_KIND_GENERIC  3  /* unaligned / ragged fallback (still on the GPU), any layout    */
+
+#define NK_MAX_SPLIT 16
+
+/* A launch plan: chosen once per (M_max, N, K) at prepare time, never inside a graph. */
+typedef struct nk_plan {
+    int32_t magic;       /* NK_PLAN_MAGIC once made                                    */
+    int32_t M_max;       /* largest M this plan accepts                                */
+    int32_t N, K;
+    int32_t kind;        /* NK_KIND_*                                                  */
+    int32_t split_k;     /* number of K slices reduced by the last-arriving CTA        */
+    int32_t k_slice;     /* K elements per slice (multiple of the kernel's K step)     */
+    int32_t tile_n;      /* weight rows per CTA                                        */
+    int32_t tile_m;      /* token rows per CTA (padded M)                              */
+    int32_t stages;      /* shared-memory pipeline depth (tensor-core kernel)          */
+    int32_t n_tiles;     /* ceil(N / tile_n)                                           */
+    int32_t m_tiles;     /* ceil(M_max / tile_m)                                       */
+    int32_t reserved[4];
+} nk_plan;
+
+#define NK_PLAN_MAGIC 0x4E4B4731 /* "NKG1" */
+
+/*
+ * Choose kernel family, split-K factor and tiles for y[M<=M_max, N] = x · Wᵀ with W [N, K].
+ *   split_k: 0 = choose automatically, else 1..16.   kind: NK_KIND_AUTO or a forced family.
+ * Replaces the implicit per-call heuristic of torch.mm/cuBLAS at the call sites listed above.
+ */
+NK_API int nk_plan_make(nk_plan* plan, int M_max, int N, int K, int split_k, int kind);
+
+/* Bytes of device workspace nk_gemm_bf16 needs for this plan (fp32 split-K partials plus
+ * one ticket word per output tile). 0 when the plan needs none. */
+NK_API size_t nk_ws_bytes(const nk_plan* plan);
+
+/* Zero a workspace once before its first use (the kernels keep it zeroed afterwards).
+ * Asynchronous on `stream`. */
+NK_API int nk_ws_init(void* ws, size_t ws_bytes, nk_stream_t stream);
+
+/*
+ * y = x · Wᵀ  (bf16 in, fp32 accumulate, bf16 out, round-to-nearest-even).
+ *   x: [M, K] with row stride ldx (elements)      — `a` of torch.mm(a, b, out=c)
+ *   w: [N, K] with row stride ldw (elements)      — storage of `b` = W.t(), strides (1, ldw)
+ *   y: [M, N] with row stride ldy (elements)      — `c`
+ * Replaces torch.mm(x, W.t(), out=y) at engine/kernels/decode.py:54,58,64,66 and
+ * engine/engine.py:114.
+ */
+NK_API int nk_gemm_bf16(const void* x, int64_t ldx,
+                 const void* w, int64_t ldw,
+                 void* y, int64_t ldy,
+                 int M, int N, int K,
+                 const nk_plan* plan, void* ws, size_t ws_bytes,
+                 nk_stream_t stream);
+
+/* Read and clear the device error word that bounded waits set on timeout (synchronizes
+ * `stream`). Writes NK_OK or NK_ERR_TIMEOUT to *status. */
+NK_API int nk_device_error(nk_stream_t stream, int* status);
+
+/* Human-readable text for a status code (static storage). */
+NK_API const char* nk_status_string(int status);
+
+/* Library version, e.g. 0x000100 for 0.1.0. */
+NK_API int nk_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NK_GEMM_H */

@@ -1,0 +1,109 @@
+"""ctypes binding of ``libnkgemm.so`` (C ABI declared in ``include/nk_gemm.h``).
+
+The library is built in-tree by ``neokernel_b200.build`` into ``neokernel_b200/lib/``. There is
+no CPU or library fallback: if the shared object is missing, importing the operator raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libnkgemm.so")
+
+# Status codes and kernel kinds (include/nk_gemm.h).
+NK_OK = 0
+NK_ERR_SHAPE = -1
+NK_ERR_ALIGN = -2
+NK_ERR_WORKSPACE = -3
+NK_ERR_SPLIT = -4
+NK_ERR_PLAN = -5
+NK_ERR_CUDA = -6
+NK_ERR_DEVICE = -7
+NK_ERR_TIMEOUT = -8
+NK_ERR_ARG = -9
+
+KIND_AUTO = 0
+KIND_GEMV = 1
+KIND_TC = 2
+KIND_GENERIC = 3
+MAX_SPLIT = 16
+PLAN_MAGIC = 0x4E4B4731
+
+# Every function the header declares; the CPU test checks the .so exports each of them.
+EXPORTS = ("nk_plan_make", "nk_ws_bytes", "nk_ws_init", "nk_gemm_bf16", "nk_device_error",
+           "nk_status_string", "nk_version")
+
+
+class NkPlan(ctypes.Structure):
+    _fields_ = [
+        ("magic", ctypes.c_int32),
+        ("M_max", ctypes.c_int32),
+        ("N", ctypes.c_int32),
+        ("K", ctypes.c_int32),
+        ("kind", ctypes.c_int32),
+        ("split_k", ctypes.c_int32),
+        ("k_slice", ctypes.c_int32),
+        ("tile_n", ctypes.c_int32),
+        ("tile_m", ctypes.c_int32),
+        ("stages", ctypes.c_int32),
+        ("n_tiles", ctypes.c_int32),
+        ("m_tiles", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 4),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_ if name != "reserved"}
+
+
+class NkError(RuntimeError):
+    """A non-zero status from libnkgemm.so."""
+
+    def __init__(self, status: int, where: str):
+        self.status = status
+        super().__init__(f"{where}: {status_string(status)} (status {status})")
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once; raise loudly if it was not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"libnkgemm.so not found at {LIB_PATH}; build it with "
+            "`python -m neokernel_b200.build` (there is no fallback implementation)")
+    L = ctypes.CDLL(LIB_PATH)
+    vp = ctypes.c_void_p
+    i32 = ctypes.c_int
+    i64 = ctypes.c_int64
+    L.nk_plan_make.argtypes = [ctypes.POINTER(NkPlan), i32, i32, i32, i32, i32]
+    L.nk_plan_make.restype = i32
+    L.nk_ws_bytes.argtypes = [ctypes.POINTER(NkPlan)]
+    L.nk_ws_bytes.restype = ctypes.c_size_t
+    L.nk_ws_init.argtypes = [vp, ctypes.c_size_t, vp]
+    L.nk_ws_init.restype = i32
+    L.nk_gemm_bf16.argtypes = [vp, i64, vp, i64, vp, i64, i32, i32, i32,
+                               ctypes.POINTER(NkPlan), vp, ctypes.c_size_t, vp]
+    L.nk_gemm_bf16.restype = i32
+    L.nk_device_error.argtypes = [vp, ctypes.POINTER(i32)]
+    L.nk_device_error.restype = i32
+    L.nk_status_string.argtypes = [i32]
+    L.nk_status_string.restype = ctypes.c_char_p
+    L.nk_version.argtypes = []
+    L.nk_version.restype = i32
+    _lib = L
+    return L
+
+
+def status_string(status: int) -> str:
+    return load().nk_status_string(int(status)).decode()
+
+
+def check(status: int, where: str) -> None:
+    if status != NK_OK:
+        raise NkError(status, where)

@@ -1,0 +1,139 @@
+"""C ABI checks that need no GPU: the library loads, exports every symbol include/nk_gemm.h
+declares, plans are made and validated on the host, and nk_gemm_bf16 rejects bad arguments
+before touching the device."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+import neokernel_b200 as nk
+from neokernel_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    names = []
+    for h in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if h.endswith(".h"):
+            src = open(os.path.join(ROOT, "include", h)).read()
+            names += re.findall(r"^NK_API\s+[\w\s\*]+?\b(nk_\w+)\s*\(", src, re.M)
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.load()
+    declared = header_functions()
+    assert declared, "no NK_API declarations found"
+    for name in declared:
+        assert hasattr(L, name), name
+    assert set(declared) == set(_lib.EXPORTS)
+    assert L.nk_version() == 0x000100
+
+
+def test_status_strings_distinct():
+    codes = [0, -1, -2, -3, -4, -5, -6, -7, -8, -9]
+    texts = [_lib.status_string(c) for c in codes]
+    assert len(set(texts)) == len(codes)
+    assert _lib.status_string(-99) == "unknown status"
+
+
+def make(M, N, K, split=0, kind=0):
+    p = _lib.NkPlan()
+    st = _lib.load().nk_plan_make(ctypes.byref(p), M, N, K, split, kind)
+    return st, p
+
+
+@pytest.mark.parametrize("args,code", [
+    ((0, 16, 16), _lib.NK_ERR_SHAPE),
+    ((1, 0, 16), _lib.NK_ERR_SHAPE),
+    ((1, 16, 0), _lib.NK_ERR_SHAPE),
+    ((1, 16, 1024, 17), _lib.NK_ERR_SPLIT),
+    ((1, 16, 1024, -1), _lib.NK_ERR_SPLIT),
+    ((1, 16, 1024, 0, 9), _lib.NK_ERR_ARG),
+    ((1, 16, 1001, 0, _lib.KIND_GEMV), _lib.NK_ERR_ALIGN),
+    ((1, 16, 1001, 2, _lib.KIND_GENERIC), _lib.NK_ERR_SPLIT),
+])
+def test_plan_make_rejects(args, code):
+    st, p = make(*args)
+    assert st == code
+    assert p.magic == 0
+
+
+@pytest.mark.parametrize("N,K", [(6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288),
+                                 (151936, 4096), (4096, 1024), (1024, 2048), (6144, 1024),
+                                 (1024, 3072), (3072, 1024), (1000, 8), (7, 2056)])
+@pytest.mark.parametrize("M", (1, 2, 3, 4, 8, 16, 17, 64, 256))
+@pytest.mark.parametrize("split", (0, 1, 3, 16))
+def test_plan_make_slices_cover_K(M, N, K, split):
+    st, p = make(M, N, K, split)
+    assert st == 0
+    assert p.magic == _lib.PLAN_MAGIC and p.M_max == M and p.N == N and p.K == K
+    assert 1 <= p.split_k <= 16
+    if split:
+        assert p.split_k <= split
+    assert (p.split_k - 1) * p.k_slice < K <= p.split_k * p.k_slice
+    assert p.k_slice % 8 == 0
+    assert p.n_tiles * p.tile_n >= N and p.m_tiles * p.tile_m >= M
+    ws = _lib.load().nk_ws_bytes(ctypes.byref(p))
+    if p.split_k == 1:
+        assert ws == 0
+    else:
+        assert ws >= p.split_k * M * N * 4 + p.n_tiles * p.m_tiles * 4
+        assert ws % 256 == 0
+
+
+def test_generic_plan_for_unaligned_K():
+    st, p = make(5, 100, 1001)
+    assert st == 0 and p.kind == _lib.KIND_GENERIC and p.split_k == 1
+
+
+def call(plan, x=0x10000, ldx=None, w=0x20000, ldw=None, y=0x30000, ldy=None, M=1, N=None,
+         K=None, ws=None, ws_bytes=0):
+    L = _lib.load()
+    N = plan.N if N is None else N
+    K = plan.K if K is None else K
+    return L.nk_gemm_bf16(x, ldx or K, w, ldw or K, y, ldy or N, M, N, K,
+                          ctypes.byref(plan) if plan is not None else None, ws, ws_bytes, None)
+
+
+def test_gemm_rejects_before_launch():
+    st, p = make(4, 4096, 1024, 1)
+    assert st == 0
+    assert call(None, N=4096, K=1024) == _lib.NK_ERR_PLAN
+    assert call(p, N=4095) == _lib.NK_ERR_PLAN
+    assert call(p, K=2048) == _lib.NK_ERR_PLAN
+    assert call(p, M=5) == _lib.NK_ERR_SHAPE
+    assert call(p, M=0) == _lib.NK_ERR_SHAPE
+    assert call(p, x=0) == _lib.NK_ERR_ARG
+    assert call(p, ldx=1000) == _lib.NK_ERR_SHAPE
+    assert call(p, x=0x10008) == _lib.NK_ERR_ALIGN       # GEMV needs 16-byte rows
+    assert call(p, ldw=1028) == _lib.NK_ERR_ALIGN
+    assert call(p, y=0x30001) == _lib.NK_ERR_ALIGN
+    st, p4 = make(4, 4096, 1024, 4)
+    assert p4.split_k == 4
+    assert call(p4) == _lib.NK_ERR_WORKSPACE
+    need = _lib.load().nk_ws_bytes(ctypes.byref(p4))
+    assert call(p4, ws=0x40000, ws_bytes=need - 1) == _lib.NK_ERR_WORKSPACE
+    assert call(p4, ws=0x40010, ws_bytes=need) == _lib.NK_ERR_ALIGN
+    corrupt = _lib.NkPlan.from_buffer_copy(p)
+    corrupt.magic = 0
+    assert call(corrupt) == _lib.NK_ERR_PLAN
+
+
+def test_python_shim_rejects_cpu_tensors():
+    import torch
+    a = torch.zeros(2, 8, dtype=torch.bfloat16)
+    w = torch.zeros(4, 8, dtype=torch.bfloat16)
+    out = torch.empty(2, 4, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        nk.mm(a, w.t(), out=out)
+    with pytest.raises(ValueError, match="bfloat16"):
+        nk.mm(a.float(), w.t(), out=out)
+
+
+def test_m_bucket():
+    assert [nk.m_bucket(m) for m in (1, 2, 3, 4, 5, 8, 9, 16, 17, 64, 100, 256)] == \
+        [1, 2, 4, 4, 8, 8, 16, 16, 32, 64, 112, 256]
