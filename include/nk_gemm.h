@@ -27,7 +27,7 @@
  *   - Launches are capture-safe: a sequence of nk_gemm_bf16 calls may be recorded into a
  *     CUDA graph and replayed, provided the workspace stays the one passed at capture.
  *   - Calls that share a workspace must be ordered (same stream, or joined by events): the
- *     split-K tickets in the workspace belong to one call at a time.
+ *     split-K tickets and partials in the workspace belong to one call at a time.
  */
 #ifndef NK_GEMM_H
 #define NK_GEMM_H
@@ -73,14 +73,18 @@ typedef struct nk_plan {
     int32_t M_max;       /* largest M this plan accepts                                */
     int32_t N, K;
     int32_t kind;        /* NK_KIND_*                                                  */
-    int32_t split_k;     /* number of K slices reduced by the last-arriving CTA        */
+    int32_t split_k;     /* K slices per tile (0 in the tensor-core family's balanced
+                            schedule, where `segments` bounds the CTAs per tile)       */
     int32_t k_slice;     /* K elements per slice (multiple of the kernel's K step)     */
     int32_t tile_n;      /* weight rows per CTA                                        */
     int32_t tile_m;      /* token rows per CTA (padded M)                              */
     int32_t stages;      /* shared-memory pipeline depth (tensor-core kernel)          */
     int32_t n_tiles;     /* ceil(N / tile_n)                                           */
     int32_t m_tiles;     /* ceil(M_max / tile_m)                                       */
-    int32_t reserved[4];
+    int32_t grid;        /* CTAs launched (tensor-core family: persistent grid)        */
+    int32_t segments;    /* most CTAs sharing one output tile (1 = no partial sums)    */
+    int32_t k_step;      /* K elements per pipeline step (tensor-core family's unit)   */
+    int32_t reserved[1];
 } nk_plan;
 
 #define NK_PLAN_MAGIC 0x4E4B4731 /* "NKG1" */
@@ -92,8 +96,12 @@ typedef struct nk_plan {
  */
 NK_API int nk_plan_make(nk_plan* plan, int M_max, int N, int K, int split_k, int kind);
 
-/* Bytes of device workspace nk_gemm_bf16 needs for this plan (fp32 split-K partials plus
- * one ticket word per output tile). 0 when the plan needs none. */
+/* Bytes of device workspace nk_gemm_bf16 needs for this plan: a fixed 256 KiB region of
+ * split-K tickets followed by the fp32 partials. 0 when the plan needs none (split_k == 1).
+ * One workspace (zeroed once by nk_ws_init) can serve any sequence of ordered calls whatever
+ * their plans, if it is as large as the largest plan needs: every plan uses the same ticket
+ * region and the kernels leave it zeroed. Plans with split_k > 1 and more than 65536 output
+ * tiles are refused (NK_ERR_SPLIT). */
 NK_API size_t nk_ws_bytes(const nk_plan* plan);
 
 /* Zero a workspace once before its first use (the kernels keep it zeroed afterwards).

@@ -10,7 +10,9 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "lib", "libnkgemm.so")
+# NK_LIB_PATH selects another build of the same library (for example one compiled with
+# different tile parameters); by default the in-tree build is used.
+LIB_PATH = os.environ.get("NK_LIB_PATH") or os.path.join(HERE, "lib", "libnkgemm.so")
 
 # Status codes and kernel kinds (include/nk_gemm.h).
 NK_OK = 0
@@ -50,7 +52,10 @@ class NkPlan(ctypes.Structure):
         ("stages", ctypes.c_int32),
         ("n_tiles", ctypes.c_int32),
         ("m_tiles", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 4),
+        ("grid", ctypes.c_int32),
+        ("segments", ctypes.c_int32),
+        ("k_step", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 1),
     ]
 
     def as_dict(self) -> dict:

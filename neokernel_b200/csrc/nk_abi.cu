@@ -44,6 +44,18 @@ static int gemv_auto_split(int tiles, int K) {
     return split;
 }
 
+// Family choice for AUTO plans, from timings on B200 of whole decode steps (graph-replayed
+// chains of the step's linears with weights far beyond L2). Past M = 1 the CUDA-core GEMV
+// needs M FMAs per weight element and the tensor-core family wins every shape. At M = 1 the
+// GEMV alone is a few percent faster on the widest weights, but in a chain of decode linears
+// the persistent tensor-core kernel overlaps each launch with the previous one (programmatic
+// dependent launch into a one-wave grid) and the all-tensor-core step is faster, so AUTO
+// keeps the GEMV for explicit requests only.
+static bool gemv_preferred(int M_max, int N, int K) {
+    (void)M_max; (void)N; (void)K;
+    return false;
+}
+
 // Round the slice to whole warp K-steps and drop slices that would be empty.
 static void set_slices(nk_plan* p, int split, int step) {
     int ks = ceil_div(p->K, split);
@@ -64,9 +76,11 @@ extern "C" int nk_plan_make(nk_plan* p, int M_max, int N, int K, int split_k, in
     if (split_k < 0 || split_k > NK_MAX_SPLIT) return NK_ERR_SPLIT;
     if (kind < NK_KIND_AUTO || kind > NK_KIND_GENERIC) return NK_ERR_ARG;
 
-    if (kind == NK_KIND_AUTO) kind = (K % 8 != 0) ? NK_KIND_GENERIC : NK_KIND_GEMV;
+    if (kind == NK_KIND_AUTO) {
+        if (K % 8 != 0) kind = NK_KIND_GENERIC;
+        else kind = gemv_preferred(M_max, N, K) ? NK_KIND_GEMV : NK_KIND_TC;
+    }
     if (kind != NK_KIND_GENERIC && K % 8 != 0) return NK_ERR_ALIGN;
-    if (kind == NK_KIND_TC) return NK_ERR_PLAN;  // tensor-core family not yet selectable
 
     p->M_max = M_max;
     p->N = N;
@@ -78,6 +92,33 @@ extern "C" int nk_plan_make(nk_plan* p, int M_max, int N, int K, int split_k, in
         p->k_slice = K;
         p->tile_n = kGenericRows;
         p->tile_m = kGenericTokens;
+    } else if (kind == NK_KIND_TC) {
+        // Persistent schedule (nk_tc.cu): one wave of CTAs, each streaming an equal run of
+        // (tile, K block) units; a forced split_k instead gives each tile split_k CTAs.
+        p->tile_m = tc_token_tile(M_max);
+        p->tile_n = kTcRowsPerCta;
+        p->stages = tc_stages(p->tile_m);
+        p->k_step = kTcKStep;
+        const int KB = ceil_div(K, kTcKStep);
+        const int64_t T = (int64_t)ceil_div(N, p->tile_n) * ceil_div(M_max, p->tile_m);
+        const int64_t U = T * KB;
+        if (split_k > 0) {
+            const int split = split_k < KB ? split_k : KB;
+            if (T * split > (int64_t)1 << 30) return NK_ERR_SHAPE;
+            p->split_k = split;
+            p->grid = (int32_t)(T * split);
+            p->segments = split;
+            p->k_slice = ceil_div(KB, split) * kTcKStep;
+        } else {
+            const int64_t slots = (int64_t)kNumSMs * tc_ctas_per_sm(p->tile_m);
+            const int64_t G = U < slots ? U : slots;
+            const int64_t q = U / G;  // units per CTA (the last ones may have one more)
+            const int64_t seg = 1 + (KB - 1 + q - 1) / q;
+            p->split_k = 0;
+            p->grid = (int32_t)G;
+            p->segments = (int32_t)(seg < G ? seg : G);
+            p->k_slice = (int32_t)(q * kTcKStep);
+        }
     } else {  // NK_KIND_GEMV
         p->tile_m = gemv_token_tile(M_max);
         p->tile_n = gemv_rows_per_cta(p->tile_m);
@@ -87,6 +128,15 @@ extern "C" int nk_plan_make(nk_plan* p, int M_max, int N, int K, int split_k, in
     }
     p->n_tiles = ceil_div(N, p->tile_n);
     p->m_tiles = ceil_div(M_max, p->tile_m);
+    if (p->kind == NK_KIND_GEMV || p->kind == NK_KIND_GENERIC) {
+        p->grid = p->n_tiles * p->split_k * p->m_tiles;
+        p->segments = p->split_k;
+        p->k_step = p->kind == NK_KIND_GEMV ? kGemvKStep : 32;
+    }
+    if (p->segments > 1 && (size_t)p->n_tiles * (size_t)p->m_tiles > kTicketsMax) {
+        memset(p, 0, sizeof(*p));
+        return NK_ERR_SPLIT;  // more output tiles than the workspace's ticket region holds
+    }
     p->magic = NK_PLAN_MAGIC;
     return NK_OK;
 }
@@ -129,9 +179,8 @@ extern "C" int nk_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t l
     a.w = static_cast<const __nv_bfloat16*>(w); a.ldw = ldw;
     a.y = static_cast<__nv_bfloat16*>(y);       a.ldy = ldy;
     a.M = M; a.N = N; a.K = K;
-    a.part = L.total ? static_cast<float*>(ws) : nullptr;
-    a.tickets = L.total ? reinterpret_cast<unsigned*>(static_cast<char*>(ws) + L.ticket_offset)
-                        : nullptr;
+    a.part = L.total ? reinterpret_cast<float*>(static_cast<char*>(ws) + L.part_offset) : nullptr;
+    a.tickets = L.total ? static_cast<unsigned*>(ws) : nullptr;
 
     cudaStream_t s = (cudaStream_t)stream;
     switch (p->kind) {

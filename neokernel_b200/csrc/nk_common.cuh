@@ -37,19 +37,35 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
 // is used by exactly one CTA once).
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
     uint4 r;
-    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
         : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
         : "l"(p));
     return r;
 }
 
-// Cached read-only 128-bit load (activations: tiny, reused by every CTA).
+// Cached read-only 128-bit load (activations: tiny, reused by every CTA). Volatile, like the
+// weight load, so neither moves across griddepcontrol.wait.
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
     uint4 r;
-    asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
         : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
         : "l"(p));
     return r;
+}
+
+// Programmatic dependent launch. A kernel launched with programmatic stream serialization
+// may start while the previous kernel on the stream is still running; it must execute
+// griddep_wait() before it reads anything that kernel writes (activations, workspace) and
+// before it writes anything that kernel may still read. Weights are read-only, so their
+// streaming may begin before the wait. Without the launch attribute both are no-ops.
+#ifndef NK_PDL
+#define NK_PDL 1  // launch with programmatic stream serialization
+#endif
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -81,24 +97,105 @@ __device__ __forceinline__ bool splitk_last_cta(unsigned* ticket, int splits) {
     return last;
 }
 
-// Workspace layout for a plan: [split][M_max][N] fp32 partials, then one ticket per
-// (m_tile, n_tile), padded to 256 bytes.
+// The last CTA's share of the split-K reduction for one output tile of `rows` weight rows
+// (from n_base) and `mcount` tokens (from m0). Thread i owns row i % rows and every
+// (blockDim.x / rows)-th token from i / rows; for G of its tokens at a time it issues the
+// loads of every slice before adding, so a batch costs about one L2 round trip instead of
+// splits x G dependent ones. Slices are summed in ascending order, as in every other path.
+template <int G, typename GemmArgsT>
+__device__ __forceinline__ void splitk_reduce_tile(const GemmArgsT& a, int n_base, int rows,
+                                                   int m0, int mcount, int splits) {
+    const int lanes = blockDim.x / rows;
+    const int r = threadIdx.x % rows;
+    const int mfirst = threadIdx.x / rows;
+    const int n = n_base + r;
+    if (n >= a.N || mfirst >= lanes) return;
+    const size_t slice = (size_t)a.M * a.N;
+    for (int mb = mfirst; mb < mcount; mb += lanes * G) {
+        float acc[G];
+#pragma unroll
+        for (int q = 0; q < G; ++q) acc[q] = 0.f;
+        const float* p = a.part + (size_t)(m0 + mb) * a.N + n;
+#pragma unroll 2
+        for (int t = 0; t < splits; ++t) {
+            float v[G];
+#pragma unroll
+            for (int q = 0; q < G; ++q)
+                v[q] = (mb + q * lanes < mcount) ? __ldcg(p + (size_t)t * slice + (size_t)q * lanes * a.N)
+                                                 : 0.f;
+#pragma unroll
+            for (int q = 0; q < G; ++q) acc[q] += v[q];
+        }
+#pragma unroll
+        for (int q = 0; q < G; ++q)
+            if (mb + q * lanes < mcount)
+                a.y[(int64_t)(m0 + mb + q * lanes) * a.ldy + n] = __float2bfloat16_rn(acc[q]);
+    }
+}
+
+// Workspace layout: a fixed region of kTicketsMax split-K tickets at offset 0, then the fp32
+// partials [split][M_max][N]. Every plan puts its tickets in the same fixed region and the
+// kernels always leave them at zero, so any sequence of ordered calls may share one
+// workspace whatever their plans (one plan's partials never overlay another's tickets).
+constexpr size_t kTicketsMax = 65536;
+constexpr size_t kTicketBytes = kTicketsMax * sizeof(unsigned);
+
 struct WsLayout {
+    size_t part_offset;
     size_t part_bytes;
-    size_t ticket_offset;
     size_t ticket_count;
     size_t total;
 };
 
 inline WsLayout ws_layout(const nk_plan& p) {
     WsLayout L{};
-    if (p.split_k <= 1) return L;
-    L.part_bytes = (size_t)p.split_k * (size_t)p.M_max * (size_t)p.N * sizeof(float);
-    L.ticket_offset = (L.part_bytes + 255) & ~(size_t)255;
     L.ticket_count = (size_t)p.n_tiles * (size_t)p.m_tiles;
-    L.total = L.ticket_offset + ((L.ticket_count * sizeof(unsigned) + 255) & ~(size_t)255);
+    L.part_offset = kTicketBytes;
+    if (p.kind == NK_KIND_TC) {
+        // [tile][segment][token column][128 rows] fp32, only when some tile is shared
+        if (p.segments <= 1) return WsLayout{};
+        const size_t cols = (size_t)(p.M_max < p.tile_m ? p.M_max : p.tile_m);
+        L.part_bytes = L.ticket_count * (size_t)p.segments * cols * 128 * sizeof(float);
+    } else {
+        // [slice][M][N] fp32
+        if (p.split_k <= 1) return WsLayout{};
+        L.part_bytes = (size_t)p.split_k * (size_t)p.M_max * (size_t)p.N * sizeof(float);
+    }
+    L.total = L.part_offset + ((L.part_bytes + 255) & ~(size_t)255);
     return L;
 }
+
+// ---------------------------------------------------------------------------------------
+// Work partition of the tensor-core family. A "unit" is one 64-wide K block of one output
+// tile (128 weight rows x NT tokens); tile t owns units [t*KB, (t+1)*KB). CTA c processes the
+// contiguous units [begin(c), begin(c+1)):
+//   balanced (split == 0): begin(c) = floor(U*c / G), so every CTA streams the same number
+//                          of weight bytes (within one block) whatever the tile count;
+//   split    (split  > 0): G = T*split and CTA c covers slice c % split of tile c / split.
+// A tile whose units span several CTAs is summed from their fp32 partials in ascending
+// rank (= ascending k) order by the CTA that finishes it last.
+// ---------------------------------------------------------------------------------------
+struct TcPartition {
+    int64_t U;   // total units
+    int KB;      // units (K blocks) per tile
+    int G;       // CTAs
+    int split;   // 0 = balanced
+
+    __host__ __device__ int64_t begin(int c) const {
+        if (split == 0) return (U * (int64_t)c) / G;
+        const int t = c / split, s = c % split;
+        return (int64_t)t * KB + ((int64_t)s * KB) / split;
+    }
+    // The CTA whose range contains unit u.
+    __host__ __device__ int cta_of(int64_t u) const {
+        if (split == 0) return (int)(((u + 1) * G + U - 1) / U - 1);
+        const int64_t t = u / KB;
+        const int64_t kb = u - t * KB;
+        return (int)(t * split + ((kb + 1) * split + KB - 1) / KB - 1);
+    }
+    __host__ __device__ int first_cta(int t) const { return cta_of((int64_t)t * KB); }
+    __host__ __device__ int last_cta(int t) const { return cta_of((int64_t)(t + 1) * KB - 1); }
+};
 
 // Launch arguments handed from the C ABI to a kernel family.
 struct GemmArgs {
@@ -108,6 +205,11 @@ struct GemmArgs {
     int M, N, K;
     float* part;            // split-K partials, or nullptr when split_k == 1
     unsigned* tickets;      // split-K tickets, or nullptr when split_k == 1
+    // tensor-core family only
+    int n_tiles;            // ceil(N / 128)
+    int segments;           // partial slots per tile
+    int part_cols;          // token columns per partial slot (min(NT, M_max))
+    TcPartition part_map;
 };
 
 int launch_gemv(const nk_plan& p, const GemmArgs& a, cudaStream_t s);
@@ -118,6 +220,16 @@ int launch_tc(const nk_plan& p, const GemmArgs& a, cudaStream_t s);
 int gemv_token_tile(int M_max);          // MT: 1, 2, 4, 8 or 16
 int gemv_rows_per_cta(int mt);           // weight rows per CTA for a given MT
 constexpr int kGemvKStep = 256;          // K elements one warp covers per 128-bit load
+int tc_token_tile(int M_max);            // NT: 16, 32, 64, 128 or 256
+int tc_stages(int nt);                   // shared-memory ring depth for a token tile
+int tc_ctas_per_sm(int nt);              // resident CTAs per SM for a token tile
+constexpr int kTcRowsPerCta = 128;       // weight rows per CTA (tcgen05 MMA M)
+constexpr int kTcBox = 64;               // K elements per TMA box (one 128-byte swizzle row)
+#ifndef NK_TC_UK
+#define NK_TC_UK 2
+#endif
+constexpr int kTcBoxesPerStage = NK_TC_UK;           // TMA boxes along K per pipeline stage
+constexpr int kTcKStep = kTcBox * kTcBoxesPerStage;  // K elements per stage (one unit)
 constexpr int kGenericRows = 8;          // rows per CTA in the generic kernel
 constexpr int kGenericTokens = 8;        // tokens per CTA in the generic kernel
 

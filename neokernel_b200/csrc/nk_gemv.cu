@@ -75,6 +75,10 @@ gemv_kernel(GemmArgs a, int k_slice, int splits) {
 #pragma unroll
         for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
 
+    if (threadIdx.x == 0) griddep_launch_dependents();
+    // The first batch of weight loads is issued before waiting for the previous kernel
+    // (weights are read-only); activations and outputs are touched only after the wait.
+    bool waited = false;
     int kk = kb;
     for (; kk + kGemvKStep * U <= ke; kk += kGemvKStep * U) {
         uint4 wv[U][R];
@@ -83,10 +87,15 @@ gemv_kernel(GemmArgs a, int k_slice, int splits) {
 #pragma unroll
             for (int r = 0; r < R; ++r)
                 wv[u][r] = ld_stream_v4(wrow[r] + kk + u * kGemvKStep + lane * 8);
+        if (!waited) {
+            griddep_wait();
+            waited = true;
+        }
 #pragma unroll
         for (int u = 0; u < U; ++u)
             gemv_accumulate<MT, R>(wv[u], xrow, a.ldx, kk + u * kGemvKStep + lane * 8, mcount, acc);
     }
+    if (!waited) griddep_wait();
     for (; kk < ke; kk += kGemvKStep) {
         const int k = kk + lane * 8;
         if (k < ke) {  // K % 8 == 0, so a chunk is either fully inside the slice or outside
@@ -122,16 +131,8 @@ gemv_kernel(GemmArgs a, int k_slice, int splits) {
 
     unsigned* ticket = a.tickets + (size_t)m_tile * gridDim.x + n_tile;
     if (splitk_last_cta(ticket, splits)) {
-        for (int i = threadIdx.x; i < BN * mcount; i += blockDim.x) {
-            const int m = i / BN;
-            const int n = n_tile * BN + (i - m * BN);
-            if (n >= a.N) continue;
-            float v = 0.f;
-            for (int t = 0; t < splits; ++t)
-                v += __ldcg(a.part + ((size_t)t * a.M + m0 + m) * a.N + n);
-            a.y[(int64_t)(m0 + m) * a.ldy + n] = __float2bfloat16_rn(v);
-        }
         if (threadIdx.x == 0) *ticket = 0u;
+        splitk_reduce_tile<2>(a, n_tile * BN, BN, m0, mcount, splits);
     }
 }
 
@@ -143,6 +144,8 @@ __global__ void __launch_bounds__(256) generic_kernel(GemmArgs a) {
     const int lane = threadIdx.x & 31;
     const int n = blockIdx.x * kGenericRows + warp;
     const int m0 = blockIdx.y * kGenericTokens;
+    if (threadIdx.x == 0) griddep_launch_dependents();
+    griddep_wait();
     if (n >= a.N) return;
     float acc[kGenericTokens];
 #pragma unroll
@@ -172,28 +175,43 @@ int gemv_token_tile(int M_max) {
 
 int gemv_rows_per_cta(int mt) { return mt <= 2 ? 16 : 32; }
 
+// Launch with programmatic stream serialization (see griddep_wait in nk_common.cuh).
+template <typename Kernel, typename... Args>
+static int launch_pdl(Kernel kernel, dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = NK_PDL ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...) == cudaSuccess ? NK_OK : NK_ERR_CUDA;
+}
+
 int launch_gemv(const nk_plan& p, const GemmArgs& a, cudaStream_t s) {
     const int mt = p.tile_m;
     const dim3 grid(p.n_tiles, p.split_k, (a.M + mt - 1) / mt);
+    const dim3 block(256);
     const int ks = p.k_slice;
     const int sp = p.split_k;
     switch (mt) {
-        case 1:  gemv_kernel<1, 2, 4><<<grid, 256, 0, s>>>(a, ks, sp); break;
-        case 2:  gemv_kernel<2, 2, 4><<<grid, 256, 0, s>>>(a, ks, sp); break;
-        case 4:  gemv_kernel<4, 4, 2><<<grid, 256, 0, s>>>(a, ks, sp); break;
-        case 8:  gemv_kernel<8, 4, 2><<<grid, 256, 0, s>>>(a, ks, sp); break;
-        case 16: gemv_kernel<16, 4, 2><<<grid, 256, 0, s>>>(a, ks, sp); break;
+        case 1:  return launch_pdl(gemv_kernel<1, 2, 4>, grid, block, s, a, ks, sp);
+        case 2:  return launch_pdl(gemv_kernel<2, 2, 4>, grid, block, s, a, ks, sp);
+        case 4:  return launch_pdl(gemv_kernel<4, 4, 2>, grid, block, s, a, ks, sp);
+        case 8:  return launch_pdl(gemv_kernel<8, 4, 2>, grid, block, s, a, ks, sp);
+        case 16: return launch_pdl(gemv_kernel<16, 4, 2>, grid, block, s, a, ks, sp);
         default: return NK_ERR_PLAN;
     }
-    return cudaGetLastError() == cudaSuccess ? NK_OK : NK_ERR_CUDA;
 }
 
 int launch_generic(const nk_plan& p, const GemmArgs& a, cudaStream_t s) {
     (void)p;
     const dim3 grid((a.N + kGenericRows - 1) / kGenericRows,
                     (a.M + kGenericTokens - 1) / kGenericTokens, 1);
-    generic_kernel<<<grid, 32 * kGenericRows, 0, s>>>(a);
-    return cudaGetLastError() == cudaSuccess ? NK_OK : NK_ERR_CUDA;
+    return launch_pdl(generic_kernel, grid, dim3(32 * kGenericRows), s, a);
 }
 
 }  // namespace nk

@@ -1,12 +1,581 @@
-// tcgen05/TMEM tensor-core family (swap-AB: weight rows are the MMA's M = 128 operand,
-// decode tokens are its N). Not selectable yet: nk_plan_make refuses NK_KIND_TC.
+// tcgen05/TMEM tensor-core family for the decode linears (sm_100a).
+//
+// Replaces the cuBLAS GEMM behind torch.mm(x, W.t(), out=y) at engine/kernels/decode.py:54,
+// 58,64,66 and engine/engine.py:114 for decode batches where CUDA-core FMA throughput, not
+// HBM, would bound the GEMV, and for the M = 64..256 tree-verify contraction.
+//
+// Swap-AB: the weight tile is the MMA's A operand (M_mma = 128 weight rows) and the decode
+// tokens are its B operand (N_mma = NT = 16..256 tokens), so a decode batch of a few tokens
+// still fills a legal MMA shape; the accumulator D[n, t] = sum_k W[n,k] x[t,k] lives in TMEM.
+//
+// Persistent schedule: the grid is one wave (148 SMs x resident CTAs) and CTA c streams the
+// contiguous run of (tile, 64-wide K block) units given by TcPartition (nk_common.cuh), so
+// every CTA moves the same number of weight bytes whatever the tile count. Six warps:
+//   warp 0 lane 0 : TMA producer. For each unit it loads the W tile [128 x 64] and the x
+//                   tile [NT x 64] (bf16, 128-byte rows, SWIZZLE_128B) into stage s of a
+//                   STAGES-deep shared-memory ring, completing on full[s].
+//   warp 1 lane 0 : MMA issuer. Per unit: four tcgen05.mma.kind::f16 (K = 16 each) into one
+//                   of two TMEM accumulators, then tcgen05.commit -> empty[s]; at the end of
+//                   each tile segment tcgen05.commit -> tfull[buf].
+//   warps 2..5    : epilogue. Warp w reads TMEM lanes 32*(w%4).. (row n of the tile) with
+//                   tcgen05.ld, frees the accumulator (tempty[buf]) and stores bf16 y when the
+//                   segment covers the whole K range; otherwise it stores an fp32 partial and
+//                   the CTA that completes the tile (ticket) sums its partials in rank order.
+// The two accumulators let the epilogue of one segment overlap the MMAs of the next.
+//
+// Programmatic dependent launch: weights do not depend on the previous kernel, so the
+// producer fills the ring with weight tiles before griddepcontrol.wait, and every CTA lets
+// the next launch begin once it is resident.
+//
+// Every mbarrier wait is bounded: on expiry the thread records NK_ERR_TIMEOUT in the device
+// error word and the CTA stops storing, drains its outstanding copies and MMAs (bounded),
+// frees its TMEM and exits. No TMA multicast is used anywhere.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "nk_common.cuh"
 
 namespace nk {
 
-int launch_tc(const nk_plan& p, const GemmArgs& a, cudaStream_t s) {
-    (void)p; (void)a; (void)s;
-    return NK_ERR_PLAN;
+constexpr int kTcRows = kTcRowsPerCta;
+constexpr int kTcUK = kTcBoxesPerStage;
+constexpr int kTcThreads = 192;            // 6 warps
+constexpr int kTcEpiThreads = 128;         // warps 2..5
+constexpr uint32_t kWaitLimit = 1u << 26;  // polls before a wait gives up (seconds)
+
+// ---------------------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity; false (error recorded) on expiry.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kWaitLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    atomicExch(&g_error, NK_ERR_TIMEOUT);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit TMEM columns -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32"
+        " {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void epi_bar() {  // named barrier over the 4 epilogue warps
+    asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiThreads) : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile stored as 128-byte rows with
+// the 128-byte swizzle (8-row x 128-byte swizzle atoms, atoms 1024 bytes apart):
+//   bits  0-13 start address >> 4     bits 16-29 leading byte offset >> 4 (unused here: 1)
+//   bits 32-45 stride byte offset >> 4 (1024 B between 8-row groups)
+//   bits 46-47 descriptor version (1 on sm_100)   bits 61-63 layout (2 = SWIZZLE_128B)
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) |
+           ((uint64_t)(1024u >> 4) << 32) | ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator (bits 4-5 = 1), A and B bf16 (bits
+// 7-9 = 1, 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bits 17-22, M >> 4 at 24-28.
+__host__ __device__ constexpr uint32_t tc_idesc(int m, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+           ((uint32_t)(m >> 4) << 24);
+}
+
+#ifndef NK_TC_SMEM_SMALL
+#define NK_TC_SMEM_SMALL (110 * 1024)  // token tiles <= 64: two CTAs per SM
+#endif
+#ifndef NK_TC_SMEM_LARGE
+#define NK_TC_SMEM_LARGE (200 * 1024)  // token tiles >= 128: one CTA per SM
+#endif
+#ifndef NK_TC_L2_PROMO
+#define NK_TC_L2_PROMO CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+#endif
+
+template <int NT>
+struct TcSmem {
+    static constexpr int kBoxA = kTcRows * kTcBox * 2;  // 16 KB: 128 weight rows x 128 B
+    static constexpr int kBoxB = NT * kTcBox * 2;       // NT tokens x 128 B
+    static constexpr int kA = kTcUK * kBoxA;
+    static constexpr int kB = kTcUK * kBoxB;
+    static constexpr int kStage = kA + kB;
+    static constexpr int kBudget = NT <= 64 ? NK_TC_SMEM_SMALL : NK_TC_SMEM_LARGE;
+    static constexpr int kStagesFit = (kBudget - 2048) / kStage;
+    static constexpr int kStages = kStagesFit > 8 ? 8 : (kStagesFit < 2 ? 2 : kStagesFit);
+    static constexpr int kBarOff = kStages * kStage;
+    static constexpr int kNumBars = 2 * kStages + 4;     // full, empty, tfull[2], tempty[2]
+    static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+    static constexpr int kBytes = kMiscOff + 16;         // tmem slot, abort flag, last flag
+    static constexpr int kAlloc = kBytes + 1024;         // slack to align the base to 1 KB
+    static constexpr int kTmemCols = 2 * NT < 32 ? 32 : 2 * NT;  // two accumulators
+    // 228 KB of shared memory per SM, 1 KB of it reserved per resident CTA
+    static constexpr int kPerSm = (233472 / (kAlloc + 1024)) > 2 ? 2 : (233472 / (kAlloc + 1024));
+    static_assert(kAlloc <= 232448, "shared-memory footprint above the 227 KB per-CTA limit");
+    static_assert(kBoxB % 1024 == 0, "activation boxes must keep 1 KB swizzle-atom alignment");
+};
+
+// One tile segment of this CTA's unit range.
+struct Segment {
+    int t;         // tile index
+    int kb0, kb1;  // K blocks [kb0, kb1) of the tile
+};
+
+__device__ __forceinline__ Segment segment_at(int64_t u, int64_t u_end, int KB) {
+    Segment sg;
+    sg.t = (int)(u / KB);
+    sg.kb0 = (int)(u - (int64_t)sg.t * KB);
+    const int64_t tile_end = (int64_t)(sg.t + 1) * KB;
+    sg.kb1 = (int)((u_end < tile_end ? u_end : tile_end) - (int64_t)sg.t * KB);
+    return sg;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kTcThreads, 1)
+tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+          GemmArgs a) {
+    using L = TcSmem<NT>;
+    constexpr int STAGES = L::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* gbase = smem_raw + (base - raw);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const TcPartition& P = a.part_map;
+    const int c = blockIdx.x;
+    const int64_t u_begin = P.begin(c);
+    const int64_t u_end = P.begin(c + 1);
+    const int n_units = (int)(u_end - u_begin);
+    const int KB = P.KB;
+
+    const uint32_t bar_full = base + L::kBarOff;
+    const uint32_t bar_empty = bar_full + STAGES * 8;
+    const uint32_t bar_tfull = bar_empty + STAGES * 8;
+    const uint32_t bar_tempty = bar_tfull + 2 * 8;
+    volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(gbase + L::kMiscOff);
+    volatile uint32_t* tmem_slot = misc;
+    volatile uint32_t* abort_flag = misc + 1;
+    volatile uint32_t* last_flag = misc + 2;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(bar_full + 8 * i, 1);
+            mbar_init(bar_empty + 8 * i, 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bar_tfull + 8 * i, 1);
+            mbar_init(bar_tempty + 8 * i, kTcEpiThreads / 32);
+        }
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tma_prefetch_desc(&tmap_w);
+        tma_prefetch_desc(&tmap_x);
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32((const void*)tmem_slot)),
+                     "r"((uint32_t)L::kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 0) griddep_launch_dependents();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            const int n_pre = n_units < STAGES ? n_units : STAGES;
+            // The first stages' weight tiles need nothing from the previous kernel.
+            for (int i = 0; i < n_pre; ++i) {
+                const int64_t u = u_begin + i;
+                const int t = (int)(u / KB);
+                const int kb = (int)(u - (int64_t)t * KB);
+                mbar_expect_tx(bar_full + 8 * i, (uint32_t)L::kStage);
+#pragma unroll
+                for (int ub = 0; ub < kTcUK; ++ub)
+                    tma_load_2d(base + i * L::kStage + ub * L::kBoxA, &tmap_w, bar_full + 8 * i,
+                                kb * kTcKStep + ub * kTcBox, (t % a.n_tiles) * kTcRows);
+            }
+            griddep_wait();
+            for (int i = 0; i < n_pre; ++i) {
+                const int64_t u = u_begin + i;
+                const int t = (int)(u / KB);
+                const int kb = (int)(u - (int64_t)t * KB);
+#pragma unroll
+                for (int ub = 0; ub < kTcUK; ++ub)
+                    tma_load_2d(base + i * L::kStage + L::kA + ub * L::kBoxB, &tmap_x,
+                                bar_full + 8 * i, kb * kTcKStep + ub * kTcBox, (t / a.n_tiles) * NT);
+            }
+            int issued = n_pre;
+            for (int i = n_pre; i < n_units; ++i) {
+                const int st = i % STAGES;
+                const uint32_t use = (uint32_t)(i / STAGES);
+                if (!mbar_wait(bar_empty + 8 * st, (use & 1u) ^ 1u)) { *abort_flag = 1u; break; }
+                if (*abort_flag) break;
+                const int64_t u = u_begin + i;
+                const int t = (int)(u / KB);
+                const int kb = (int)(u - (int64_t)t * KB);
+                const uint32_t sa = base + st * L::kStage;
+                mbar_expect_tx(bar_full + 8 * st, (uint32_t)L::kStage);
+#pragma unroll
+                for (int ub = 0; ub < kTcUK; ++ub)
+                    tma_load_2d(sa + ub * L::kBoxA, &tmap_w, bar_full + 8 * st,
+                                kb * kTcKStep + ub * kTcBox, (t % a.n_tiles) * kTcRows);
+#pragma unroll
+                for (int ub = 0; ub < kTcUK; ++ub)
+                    tma_load_2d(sa + L::kA + ub * L::kBoxB, &tmap_x, bar_full + 8 * st,
+                                kb * kTcKStep + ub * kTcBox, (t / a.n_tiles) * NT);
+                ++issued;
+            }
+            // Drain: every stage's last load has landed and (unless the MMA issuer gave up)
+            // every MMA that read it has completed before this CTA may exit.
+            for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i) {
+                const int st = i % STAGES;
+                const uint32_t use = (uint32_t)(i / STAGES);
+                mbar_wait(bar_full + 8 * st, use & 1u);
+                if (*abort_flag == 0u) mbar_wait(bar_empty + 8 * st, use & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = tc_idesc(kTcRows, NT);
+            int i = 0, seg = 0;
+            for (int64_t u = u_begin; u < u_end; ++seg) {
+                const Segment sg = segment_at(u, u_end, KB);
+                const int buf = seg & 1;
+                const uint32_t use_b = (uint32_t)(seg >> 1);
+                if (!mbar_wait(bar_tempty + 8 * buf, (use_b & 1u) ^ 1u)) { *abort_flag = 1u; break; }
+                tc_fence_after();
+                const uint32_t dacc = tmem + (uint32_t)(buf * NT);
+                bool stop = false;
+                for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++i) {
+                    const int st = i % STAGES;
+                    const uint32_t use = (uint32_t)(i / STAGES);
+                    if (!mbar_wait(bar_full + 8 * st, use & 1u)) { stop = true; break; }
+                    tc_fence_after();
+                    const uint32_t sa = base + st * L::kStage;
+                    const uint32_t sb = sa + L::kA;
+#pragma unroll
+                    for (int ub = 0; ub < kTcUK; ++ub)
+#pragma unroll
+                        for (int j = 0; j < kTcBox / 16; ++j)  // 32 bytes of K per MMA
+                            tc_mma(dacc, sw128_desc(sa + ub * L::kBoxA + 32 * j),
+                                   sw128_desc(sb + ub * L::kBoxB + 32 * j), idesc,
+                                   (kb > sg.kb0 || ub > 0 || j > 0) ? 1u : 0u);
+                    tc_commit(bar_empty + 8 * st);
+                }
+                tc_commit(bar_tfull + 8 * buf);  // arrives when this segment's MMAs are done
+                if (stop) { *abort_flag = 1u; break; }
+                u += sg.kb1 - sg.kb0;
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        griddep_wait();
+        const int ep = threadIdx.x - 64;          // 0..127
+        const int q = warp & 3;                   // TMEM lane quarter this warp may access
+        const int row = 32 * q + lane;            // tile row owned by this thread
+        const uint32_t tlane = (uint32_t)(32 * q) << 16;
+        int seg = 0;
+        for (int64_t u = u_begin; u < u_end; ++seg) {
+            const Segment sg = segment_at(u, u_end, KB);
+            u += sg.kb1 - sg.kb0;
+            const int buf = seg & 1;
+            const int n = (sg.t % a.n_tiles) * kTcRows + row;
+            const int m0 = (sg.t / a.n_tiles) * NT;
+            const int mcount = min(NT, a.M - m0);
+            const bool whole = (sg.kb0 == 0 && sg.kb1 == KB);
+            const bool ok = mbar_wait(bar_tfull + 8 * buf, (uint32_t)(seg >> 1) & 1u) &&
+                            *abort_flag == 0u;
+            tc_fence_after();
+            const uint32_t taddr = tmem + (uint32_t)(buf * NT) + tlane;
+            const int rank = c - P.first_cta(sg.t);
+            float* dst = a.part + (((size_t)sg.t * a.segments + rank) * a.part_cols) * kTcRows + row;
+            if (ok) {
+#pragma unroll 1
+                for (int c0 = 0; c0 < NT; c0 += 16) {
+                    if (c0 >= mcount) break;  // warp-uniform
+                    float v[16];
+                    tmem_ld16(taddr + c0, v);
+                    if (whole) {
+                        if (n < a.N) {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                if (c0 + j < mcount)
+                                    a.y[(int64_t)(m0 + c0 + j) * a.ldy + n] = __float2bfloat16_rn(v[j]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (c0 + j < mcount) dst[(size_t)(c0 + j) * kTcRows] = v[j];
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_tempty + 8 * buf);
+            if (!whole) {
+                // Partial segment: the CTA whose arrival completes the tile sums all partials
+                // of the tile in ascending rank (= ascending k) order.
+                __threadfence();
+                epi_bar();
+                const int nseg = P.last_cta(sg.t) - P.first_cta(sg.t) + 1;
+                if (ep == 0) {
+                    const unsigned prev = atomicAdd(a.tickets + sg.t, 1u);
+                    *last_flag = (prev == (unsigned)(nseg - 1)) ? 1u : 0u;
+                }
+                epi_bar();
+                if (*last_flag) {
+                    __threadfence();
+                    const float* src =
+                        a.part + ((size_t)sg.t * a.segments * a.part_cols) * kTcRows + row;
+                    if (n < a.N && *abort_flag == 0u) {
+                        for (int c0 = 0; c0 < mcount; c0 += 8) {
+                            float acc[8];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll 2
+                            for (int r = 0; r < nseg; ++r) {
+                                const float* pr = src + ((size_t)r * a.part_cols + c0) * kTcRows;
+                                float v[8];
+#pragma unroll
+                                for (int j = 0; j < 8; ++j)
+                                    v[j] = (c0 + j < mcount) ? __ldcg(pr + (size_t)j * kTcRows) : 0.f;
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) acc[j] += v[j];
+                            }
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                if (c0 + j < mcount)
+                                    a.y[(int64_t)(m0 + c0 + j) * a.ldy + n] = __float2bfloat16_rn(acc[j]);
+                        }
+                    }
+                    if (ep == 0) a.tickets[sg.t] = 0u;
+                }
+                epi_bar();  // last_flag is rewritten by the next partial segment
+            }
+        }
+    }
+
+    // ---------------- teardown ----------------
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"((uint32_t)L::kTmemCols)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static int get_encoder() {
+    if (g_encode) return NK_OK;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+        return NK_ERR_CUDA;
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    return NK_OK;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with row stride ld (elements),
+// box [box_rows, 64 columns], 128-byte swizzle; out-of-range rows and columns read as zero.
+static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld,
+                    int box_rows) {
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    cuuint32_t box[2] = {(cuuint32_t)kTcBox, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, (CUtensorMapL2promotion)NK_TC_L2_PROMO,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? NK_OK : NK_ERR_ALIGN;
+}
+
+int tc_token_tile(int M_max) {
+    if (M_max <= 16) return 16;
+    if (M_max <= 32) return 32;
+    if (M_max <= 64) return 64;
+    if (M_max <= 128) return 128;
+    return 256;
+}
+
+int tc_stages(int nt) {
+    switch (nt) {
+        case 16: return TcSmem<16>::kStages;
+        case 32: return TcSmem<32>::kStages;
+        case 64: return TcSmem<64>::kStages;
+        case 128: return TcSmem<128>::kStages;
+        default: return TcSmem<256>::kStages;
+    }
+}
+
+#ifndef NK_TC_GRID_PER_SM
+#define NK_TC_GRID_PER_SM 0  // 0: as many CTAs per SM as shared memory allows
+#endif
+
+int tc_ctas_per_sm(int nt) {
+    if (NK_TC_GRID_PER_SM > 0) return NK_TC_GRID_PER_SM;
+    switch (nt) {
+        case 16: return TcSmem<16>::kPerSm;
+        case 32: return TcSmem<32>::kPerSm;
+        case 64: return TcSmem<64>::kPerSm;
+        case 128: return TcSmem<128>::kPerSm;
+        default: return TcSmem<256>::kPerSm;
+    }
+}
+
+template <int NT>
+static int launch_tc_t(int grid, const GemmArgs& a, const CUtensorMap& mw, const CUtensorMap& mx,
+                       cudaStream_t s) {
+    using L = TcSmem<NT>;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return NK_ERR_CUDA;
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 L::kAlloc) != cudaSuccess)
+            return NK_ERR_CUDA;
+        attr_set[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.dynamicSmemBytes = L::kAlloc;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = NK_PDL ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, tc_kernel<NT>, mw, mx, a) == cudaSuccess ? NK_OK
+                                                                                      : NK_ERR_CUDA;
+}
+
+int launch_tc(const nk_plan& p, const GemmArgs& in, cudaStream_t s) {
+    if (get_encoder() != NK_OK) return NK_ERR_CUDA;
+    GemmArgs a = in;
+    const int nt = p.tile_m;
+    const int KB = (a.K + kTcKStep - 1) / kTcKStep;
+    const int m_tiles = (a.M + nt - 1) / nt;  // token tiles of this call (<= the plan's)
+    a.n_tiles = p.n_tiles;
+    a.segments = p.segments;
+    a.part_cols = p.M_max < nt ? p.M_max : nt;
+    TcPartition& P = a.part_map;
+    P.KB = KB;
+    P.U = (int64_t)p.n_tiles * m_tiles * KB;
+    P.split = p.split_k;
+    if (p.split_k > 0) {
+        P.G = p.n_tiles * m_tiles * p.split_k;
+    } else {
+        // Keep at least the plan's units per CTA, so no tile is shared by more CTAs than the
+        // plan's `segments` (the workspace was sized for that).
+        const int64_t U_plan = (int64_t)p.n_tiles * p.m_tiles * KB;
+        const int64_t q = U_plan / p.grid;
+        int64_t G = P.U / q;
+        if (G > p.grid) G = p.grid;
+        if (G < 1) G = 1;
+        P.G = (int)G;
+    }
+    CUtensorMap mw, mx;
+    if (make_map(&mw, a.w, a.N, a.K, a.ldw, kTcRows) != NK_OK) return NK_ERR_ALIGN;
+    if (make_map(&mx, a.x, a.M, a.K, a.ldx, nt) != NK_OK) return NK_ERR_ALIGN;
+    switch (nt) {
+        case 16: return launch_tc_t<16>(P.G, a, mw, mx, s);
+        case 32: return launch_tc_t<32>(P.G, a, mw, mx, s);
+        case 64: return launch_tc_t<64>(P.G, a, mw, mx, s);
+        case 128: return launch_tc_t<128>(P.G, a, mw, mx, s);
+        case 256: return launch_tc_t<256>(P.G, a, mw, mx, s);
+        default: return NK_ERR_PLAN;
+    }
 }
 
 }  // namespace nk

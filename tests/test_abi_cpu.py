@@ -71,6 +71,9 @@ def test_plan_make_slices_cover_K(M, N, K, split):
     st, p = make(M, N, K, split)
     assert st == 0
     assert p.magic == _lib.PLAN_MAGIC and p.M_max == M and p.N == N and p.K == K
+    if p.kind == _lib.KIND_TC:
+        check_tc_partition(p, M)
+        return
     assert 1 <= p.split_k <= 16
     if split:
         assert p.split_k <= split
@@ -81,8 +84,85 @@ def test_plan_make_slices_cover_K(M, N, K, split):
     if p.split_k == 1:
         assert ws == 0
     else:
-        assert ws >= p.split_k * M * N * 4 + p.n_tiles * p.m_tiles * 4
+        assert ws >= 262144 + p.split_k * M * N * 4
+        assert p.n_tiles * p.m_tiles <= 65536
         assert ws % 256 == 0
+
+
+def test_forced_split_with_too_many_tiles_is_refused():
+    st, p = make(16, 151936 * 16, 4096, 4, _lib.KIND_GEMV)  # 75968 tiles > 65536 tickets
+    assert st == _lib.NK_ERR_SPLIT and p.magic == 0
+    st, p = make(1, 151936, 4096, 4, _lib.KIND_GEMV)       # 9496 tiles fit
+    assert st == 0 and p.split_k == 4
+
+
+class Partition:
+    """Python mirror of TcPartition (neokernel_b200/csrc/nk_common.cuh)."""
+
+    def __init__(self, U, KB, G, split):
+        self.U, self.KB, self.G, self.split = U, KB, G, split
+
+    def begin(self, c):
+        if self.split == 0:
+            return (self.U * c) // self.G
+        t, s = divmod(c, self.split)
+        return t * self.KB + (s * self.KB) // self.split
+
+    def cta_of(self, u):
+        if self.split == 0:
+            return ((u + 1) * self.G + self.U - 1) // self.U - 1
+        t, kb = divmod(u, self.KB)
+        return t * self.split + ((kb + 1) * self.split + self.KB - 1) // self.KB - 1
+
+
+def launch_partition(p, M):
+    """The partition launch_tc (nk_tc.cu) builds for a call with M tokens."""
+    KB = -(-p.K // p.k_step)
+    m_tiles = -(-M // p.tile_m)
+    U = p.n_tiles * m_tiles * KB
+    if p.split_k:
+        return Partition(U, KB, p.n_tiles * m_tiles * p.split_k, p.split_k)
+    q = (p.n_tiles * p.m_tiles * KB) // p.grid
+    G = max(1, min(p.grid, U // q))
+    return Partition(U, KB, G, 0)
+
+
+def check_tc_partition(p, M_max):
+    assert p.tile_n == 128 and p.tile_m in (16, 32, 64, 128, 256) and p.grid >= 1
+    assert p.k_step % 64 == 0
+    if not p.split_k:
+        assert p.grid <= 148 * 2
+    for M in sorted({1, M_max, max(1, M_max // 2)}):
+        P = launch_partition(p, M)
+        assert P.begin(0) == 0 and P.begin(P.G) == P.U
+        cover = []
+        for c in range(P.G):
+            b, e = P.begin(c), P.begin(c + 1)
+            assert e > b, "empty CTA range"
+            assert P.cta_of(b) == c and P.cta_of(e - 1) == c
+            cover.append(e - b)
+        assert sum(cover) == P.U
+        assert max(cover) - min(cover) <= (1 if not P.split else P.KB)
+        T = P.U // P.KB
+        for t in range(T):
+            nseg = P.cta_of((t + 1) * P.KB - 1) - P.cta_of(t * P.KB) + 1
+            assert 1 <= nseg <= p.segments, (t, nseg, p.segments)
+
+
+@pytest.mark.parametrize("N,K", [(6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288),
+                                 (151936, 4096), (1024, 2048), (777, 520), (130, 64), (8, 8)])
+@pytest.mark.parametrize("M", (1, 4, 16, 17, 64, 100, 256, 300))
+@pytest.mark.parametrize("split", (0, 1, 2, 7, 16))
+def test_tc_partition_covers_units_once(M, N, K, split):
+    st, p = make(M, N, K, split, _lib.KIND_TC)
+    assert st == 0 and p.kind == _lib.KIND_TC
+    check_tc_partition(p, M)
+    ws = _lib.load().nk_ws_bytes(ctypes.byref(p))
+    if p.segments > 1:
+        cols = min(M, p.tile_m)
+        assert ws >= 262144 + p.n_tiles * p.m_tiles * p.segments * cols * 128 * 4
+    else:
+        assert ws == 0
 
 
 def test_generic_plan_for_unaligned_K():

@@ -195,6 +195,39 @@ def test_split_k_sweep(M, N, K):
     assert 1 in seen and len(seen) >= 4
 
 
+@pytest.mark.parametrize("kind", (nk.KIND_GEMV, nk.KIND_TC))
+@pytest.mark.parametrize("M", (1, 2, 3, 4, 8, 16))
+@pytest.mark.parametrize("N,K", [(100, 1000), (513, 2056), (4096, 1024), (1024, 3072), (130, 64)])
+def test_families_vs_oracle(kind, M, N, K):
+    W = synthetic.weight(N, K, seed=N * 3 + K).to(DEV)
+    x = synthetic.activation(M, K, seed=M * 5 + K).to(DEV)
+    for split in (0, 1, 3):
+        y = run(x, W, nk.plan_for(M, N, K, kind=kind, split_k=split))
+        assert_vs_oracle(y, x, W)
+
+
+@pytest.mark.parametrize("M", (17, 32, 33, 64, 100, 128, 200, 256, 300))
+@pytest.mark.parametrize("N,K", [(4096, 1024), (777, 520), (256, 4096)])
+def test_tc_token_tiles_vs_oracle(M, N, K):
+    W = synthetic.weight(N, K, seed=N + 2 * K).to(DEV)
+    x = synthetic.activation(M, K, seed=M + 3 * K).to(DEV)
+    for split in (0, 1, 2):
+        plan = nk.plan_for(M, N, K, kind=nk.KIND_TC, split_k=split)
+        assert plan.kind == nk.KIND_TC
+        assert_vs_oracle(run(x, W, plan), x, W)
+
+
+@pytest.mark.parametrize("N,K", Q8B[:4] + [(151936, 4096)])
+@pytest.mark.parametrize("M", (1, 4, 8, 16))
+def test_tc_decode_shapes_vs_fp32(M, N, K):
+    W = weight_dev(N, K, seed=N + K)
+    x = synthetic.activation(M, K, seed=M + 1, device=DEV)
+    y = run(x, W, nk.plan_for(M, N, K, kind=nk.KIND_TC))
+    assert (y.float() - fp32_ref(x, W)).abs().max().item() <= oracle.tolerance(K)
+    y2 = run(x, W, nk.plan_for(M, N, K, kind=nk.KIND_GEMV))
+    assert (y.float() - y2.float()).abs().max().item() <= oracle.tolerance(K)
+
+
 @pytest.mark.parametrize("M", (64, 128, 256))
 @pytest.mark.parametrize("N,K", [(6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288)])
 def test_verify_shapes(M, N, K):
@@ -208,11 +241,12 @@ def test_deterministic_across_runs():
     N, K, M = 4096, 12288, 4
     W = weight_dev(N, K, seed=N + K)
     x = synthetic.activation(M, K, seed=9, device=DEV)
-    for split in (1, 5, 10):
-        plan = nk.plan_for(M, N, K, split_k=split)
-        a = run(x, W, plan)
-        b = run(x, W, plan)
-        assert torch.equal(a, b)
+    for kind in (nk.KIND_GEMV, nk.KIND_TC):
+        for split in (1, 5, 10):
+            plan = nk.plan_for(M, N, K, kind=kind, split_k=split)
+            a = run(x, W, plan)
+            b = run(x, W, plan)
+            assert torch.equal(a, b)
 
 
 def test_cuda_graph_capture_and_replay():
