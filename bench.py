@@ -242,9 +242,14 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--single", default=None,
+                    help="N,K,M: run one decode linear --reps times and exit (profiler captures)")
+    ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.single:
+        return single(args)
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
 
@@ -422,6 +427,24 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+    return 0
+
+
+def single(args):
+    """One decode linear y[M,N] = x[M,K] W[N,K]^T, launched --reps times on cuda:0 with the
+    plan --kind/--split select (a small, self-contained case for ncu captures)."""
+    import neokernel_b200 as nk
+    from neokernel_b200 import synthetic
+    N, K, M = (int(v) for v in args.single.split(","))
+    dev = torch.device("cuda", 0)
+    W = synthetic.weight(N, K, seed=1, device=dev)
+    x = synthetic.activation(M, K, seed=2, device=dev)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    plan = nk.plan_for(M, N, K, kind=args.kind, split_k=args.split)
+    for _ in range(args.reps):
+        nk.mm(x, W.t(), out=y, plan=plan)
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"single": [N, K, M], "reps": args.reps, "plan": plan.as_dict()}))
     return 0
 
 
