@@ -123,6 +123,31 @@ NK_API int nk_gemm_bf16(const void* x, int64_t ldx,
                  const nk_plan* plan, void* ws, size_t ws_bytes,
                  nk_stream_t stream);
 
+/*
+ * y = x · Wᵀ exactly as nk_gemm_bf16, for callers that cannot allocate device memory, so
+ * cannot hand the library a workspace: an operator inside a host framework that owns every
+ * device allocation and passes it only its inputs and outputs, a process whose device-memory
+ * budget is fixed at start-up, or a latency-critical path that avoids cudaMalloc because a
+ * device allocation serializes work in flight on other streams. No counterpart in the
+ * reference: its torch.mm call sites let the library allocate as it pleases.
+ *
+ * The split-K scratch comes from an array of NK_STATIC_SCRATCH_BYTES (8 MiB) compiled into
+ * the library, which every GPU that loads it holds until the process exits. Only plans of
+ * the tensor-core family (NK_KIND_TC, what AUTO plans choose for aligned shapes) are taken
+ * (else NK_ERR_PLAN); a plan whose nk_ws_bytes() exceeds the array is refused with
+ * NK_ERR_WORKSPACE. Nothing is allocated. The first call on each device (with that device
+ * current) looks up the array's device address, so make it before any stream capture on that
+ * device. All calls on a device share the array and it keeps the last call's contents: each
+ * call clears the tickets it uses, and calls that overlap on the GPU race — order them (one
+ * stream, or streams joined by events).
+ */
+#define NK_STATIC_SCRATCH_BYTES (8u << 20)
+NK_API int nk_gemm_bf16_static(const void* x, int64_t ldx,
+                               const void* w, int64_t ldw,
+                               void* y, int64_t ldy,
+                               int M, int N, int K,
+                               const nk_plan* plan, nk_stream_t stream);
+
 /* Read and clear the device error word that bounded waits set on timeout (synchronizes
  * `stream`). Writes NK_OK or NK_ERR_TIMEOUT to *status. */
 NK_API int nk_device_error(nk_stream_t stream, int* status);

@@ -35,7 +35,7 @@ PLAN_MAGIC = 0x4E4B4731
 
 # Every function the header declares; the CPU test checks the .so exports each of them.
 EXPORTS = ("nk_plan_make", "nk_ws_bytes", "nk_ws_init", "nk_gemm_bf16", "nk_device_error",
-           "nk_status_string", "nk_version")
+           "nk_status_string", "nk_version", "nk_gemm_bf16_static")
 
 
 class NkPlan(ctypes.Structure):

@@ -4,3 +4,4 @@
 #include "nk_gemv.cu"
 #include "nk_tc.cu"
 #include "nk_abi.cu"
+#include "nk_static.cu"
