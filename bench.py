@@ -242,6 +242,9 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="skip the 36-layer Qwen3-8B decode-step tok/s measurement")
+    ap.add_argument("--decode-batches", default="1,16")
     ap.add_argument("--single", default=None,
                     help="N,K,M: run one decode linear --reps times and exit (profiler captures)")
     ap.add_argument("--reps", type=int, default=3)
@@ -394,6 +397,11 @@ def main():
     if not args.no_e2e:
         e2e = e2e_pass(nk, lin, Ws, m_list, plans, dev, stream, args, world, local)
 
+    decode = None
+    if not args.no_decode:
+        decode = decode_bench(nk, dev, [int(b) for b in args.decode_batches.split(",")],
+                              world, local)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference(m_list, budget_s=args.cpu_budget)
@@ -417,6 +425,7 @@ def main():
             "cpu_baseline": ({k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
                              if cpu else None),
             "e2e": e2e,
+            "decode": decode,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
         }
@@ -446,6 +455,44 @@ def single(args):
     torch.cuda.synchronize(dev)
     print(json.dumps({"single": [N, K, M], "reps": args.reps, "plan": plan.as_dict()}))
     return 0
+
+
+def decode_bench(nk, dev, batches, world, local, kv=1024, steps=20, warmup=3):
+    """Decode tokens/s of the full Qwen3-8B step (36 layers, random init, CUDA graph) at KV
+    length 1024, with the decode linears on neokernel_b200.mm and, for comparison in the same
+    harness, on torch.mm (cuBLAS, the reference's call). Non-linear ops are PyTorch in both."""
+    from neokernel_b200 import qwen3
+    w = qwen3.Qwen3Weights(qwen3.QWEN3_8B, seed=7, device=dev)
+    out = {"model": "qwen3-8b random-init, 36 layers, vocab 151936", "kv_length": kv,
+           "steps": steps, "timing": "CUDA events around graph replays, max over ranks"}
+    for name, linear in (("neokernel_b200", nk.mm), ("torch_mm", torch.mm)):
+        res = {}
+        for B in batches:
+            g = qwen3.GraphDecoder(w, B, kv + warmup + steps + 1, linear, device=dev)
+            gen = torch.Generator(device=dev).manual_seed(B)
+            for c in g.st.k_cache + g.st.v_cache:
+                c.normal_(generator=gen)
+            g.st.position.fill_(kv)
+            g.st.tokens.copy_(torch.randint(0, qwen3.QWEN3_8B.vocab, (B,), generator=gen, device=dev))
+            for _ in range(warmup):
+                g.step()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier(world)
+            torch.cuda.synchronize(dev)
+            a.record()
+            for _ in range(steps):
+                g.step()
+            b.record()
+            b.synchronize()
+            ms = max_over_ranks(a.elapsed_time(b), world, local) / steps
+            res[str(B)] = {"ms_per_token_step": round(ms, 4),
+                           "tok_s": round(B * world / (ms / 1e3), 1)}
+            del g
+            torch.cuda.empty_cache()
+        out[name] = res
+    del w
+    torch.cuda.empty_cache()
+    return out
 
 
 def _traffic_per_launch(avg_bytes):

@@ -1,0 +1,96 @@
+"""Decode-step parity: the Qwen3 decode graph with the decode linears on neokernel_b200.mm
+against the same graph on torch.mm (the reference's own call, engine/kernels/decode.py:54-66,
+engine/engine.py:114), random-init weights, CUDA-graph replay.
+
+Greedy tokens are compared over 128 generated tokens. Random-init models have near-flat
+logits (top-2 gaps of a few hundredths among 151,936 entries), so a flip is legitimate only
+where the reference's own logits were within rounding of a tie: every step where the tokens
+differ must pass the reference judge's margin rule (neokernel/judge.py:71-86) — the token we
+chose scores within 2.0 of the maximum of the torch.mm path's teacher-forced logits — and in
+practice within a few bf16 ulps. Identical-token counts are printed.
+"""
+
+import json
+
+import pytest
+import torch
+
+import neokernel_b200 as nk
+from neokernel_b200 import qwen3
+
+pytestmark = pytest.mark.gpu
+
+MARGIN = 2.0  # neokernel/judge.py MARGIN, used by check_logits (judge.py:71-86)
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _no_tf32():
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = old
+
+
+def margins(ref_logits, tokens):
+    """max(ref) - ref[chosen] per (b, t), as check_logits computes it."""
+    best = ref_logits.max(dim=-1).values
+    chosen = ref_logits.gather(-1, tokens.unsqueeze(-1)).squeeze(-1)
+    return best - chosen
+
+
+def test_two_layer_step_matches_torch_mm():
+    d = qwen3.QWEN3_8B
+    w = qwen3.Qwen3Weights(d, seed=3, layers=2)
+    B, cap = 4, 64
+    ours = qwen3.DecodeState(w, B, cap)
+    ref = qwen3.DecodeState(w, B, cap)
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    for pos in range(6):
+        toks = torch.randint(0, d.vocab, (B,), generator=gen, device="cuda")
+        for st in (ours, ref):
+            st.tokens.copy_(toks)
+            st.position.fill_(pos)
+        qwen3.decode_step(ours, w, nk.mm)
+        qwen3.decode_step(ref, w, torch.mm)
+        torch.cuda.synchronize()
+        diff = (ours.logits.float() - ref.logits.float()).abs().max().item()
+        scale = ref.logits.float().abs().max().item()
+        assert diff <= 0.02 * scale, (pos, diff, scale)
+        for a, b in zip(ours.k_cache + ours.v_cache, ref.k_cache + ref.v_cache):
+            assert (a.float() - b.float()).abs().max().item() <= 0.05
+
+
+@pytest.mark.parametrize("batch", (1, 4))
+def test_qwen3_8b_128_greedy_tokens(batch):
+    d = qwen3.QWEN3_8B
+    w = qwen3.Qwen3Weights(d, seed=11)
+    prompt_len, new = 8, 128
+    cap = prompt_len + new
+    gen = torch.Generator(device="cuda").manual_seed(20260922)
+    prompt = torch.randint(0, d.vocab, (batch, prompt_len), generator=gen, device="cuda")
+
+    ours = qwen3.GraphDecoder(w, batch, cap, nk.mm)
+    ref = qwen3.GraphDecoder(w, batch, cap, torch.mm)
+    t_ours = ours.greedy(prompt, new)
+    t_ref = ref.greedy(prompt, new)
+    torch.cuda.synchronize()
+    same = (t_ours == t_ref)
+    # Teacher-forced replay of our tokens on the reference path (the judge's check).
+    ref_logits = ref.teacher_forced_logits(prompt, t_ours)
+    m = margins(ref_logits, t_ours)
+    first_diff = [int(same[b].logical_not().nonzero()[0]) if not same[b].all() else None
+                  for b in range(batch)]
+    report = {"test": f"qwen3-8b/greedy/B{batch}", "identical_tokens": int(same.sum()),
+              "tokens": batch * new, "first_divergence": first_diff,
+              "worst_margin": float(m.max()), "mean_margin": float(m.mean())}
+    print(json.dumps(report), flush=True)
+    assert torch.isfinite(ref_logits).all()
+    assert float(m.max()) <= MARGIN, report
+    # Up to its first divergence a sequence has seen identical inputs on both paths, so the
+    # token that differs there must be a near-tie of the reference's own logits: within a
+    # few bf16 ulps (ulp = 1/32 for logits in [4, 8)).
+    for b in range(batch):
+        if first_diff[b] is not None:
+            assert float(m[b, first_diff[b]]) <= 0.125, report
+    del ours, ref
+    torch.cuda.empty_cache()
