@@ -245,6 +245,9 @@ def main():
     ap.add_argument("--no-decode", action="store_true",
                     help="skip the 36-layer Qwen3-8B decode-step tok/s measurement")
     ap.add_argument("--decode-batches", default="1,16")
+    ap.add_argument("--tp-decode", choices=("auto", "on", "off"), default="auto",
+                    help="Qwen3-32B tensor-parallel decode tok/s (auto: only when N > 1)")
+    ap.add_argument("--tp-batches", default="1,8,32")
     ap.add_argument("--single", default=None,
                     help="N,K,M: run one decode linear --reps times and exit (profiler captures)")
     ap.add_argument("--reps", type=int, default=3)
@@ -402,6 +405,11 @@ def main():
         decode = decode_bench(nk, dev, [int(b) for b in args.decode_batches.split(",")],
                               world, local)
 
+    tp_decode = None
+    if args.tp_decode == "on" or (args.tp_decode == "auto" and world > 1):
+        tp_decode = tp_decode_bench(nk, dev, [int(b) for b in args.tp_batches.split(",")],
+                                    world, rank, local)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference(m_list, budget_s=args.cpu_budget)
@@ -426,6 +434,7 @@ def main():
                              if cpu else None),
             "e2e": e2e,
             "decode": decode,
+            "tp_decode": tp_decode,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
         }
@@ -493,6 +502,48 @@ def decode_bench(nk, dev, batches, world, local, kv=1024, steps=20, warmup=3):
     del w
     torch.cuda.empty_cache()
     return out
+
+
+def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, warmup=3):
+    """Qwen3-32B-shaped tensor-parallel decode (64 layers, random init) over the N ranks of
+    this run: QKV/gate_up split by column, o_proj/down by K with an fp32 NCCL all-reduce,
+    lm_head by vocabulary; one CUDA graph per batch; KV length 2048. tok/s counts each
+    sequence's token once (the ranks share one model)."""
+    from neokernel_b200 import qwen3, tp
+    d = qwen3.QWEN3_32B
+    w = tp.TPWeights(d, seed=13, rank=rank, world=world, device=dev)
+    res = {}
+    for B in batches:
+        g = qwen3.GraphDecoder(w, B, kv + warmup + steps + 1, nk.mm, device=dev,
+                               make_hooks=tp.make_hooks(w))
+        gen = torch.Generator(device=dev).manual_seed(100 + B)
+        for c in g.st.k_cache + g.st.v_cache:
+            c.normal_(generator=gen)
+        g.st.position.fill_(kv)
+        g.st.tokens.copy_(torch.randint(0, d.vocab, (B,), generator=torch.Generator(
+            device=dev).manual_seed(B), device=dev))  # same tokens on every rank
+        for _ in range(warmup):
+            g.step()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        a.record()
+        for _ in range(steps):
+            g.step()
+        b.record()
+        b.synchronize()
+        ms = max_over_ranks(a.elapsed_time(b), world, local) / steps
+        res[str(B)] = {"ms_per_token_step": round(ms, 3), "tok_s": round(B / (ms / 1e3), 1)}
+        barrier(world)
+        del g.graph  # NCCL-holding graph released before anything tears down the group
+        del g
+        torch.cuda.empty_cache()
+    del w
+    torch.cuda.empty_cache()
+    return {"model": "qwen3-32b random-init, 64 layers, hidden 5120, MLP 25600, 64Q/8KV x 128",
+            "tp": world, "kv_length": kv, "steps": steps, "batches": res,
+            "collectives": "fp32 all-reduce after o_proj and down, all-gather of (max, index) "
+                           "for the vocab-split argmax; NCCL, captured in the CUDA graph"}
 
 
 def _traffic_per_launch(avg_bytes):

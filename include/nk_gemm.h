@@ -148,6 +148,21 @@ NK_API int nk_gemm_bf16_static(const void* x, int64_t ldx,
                                int M, int N, int K,
                                const nk_plan* plan, nk_stream_t stream);
 
+/*
+ * y32 = x · Wᵀ with fp32 accumulation and NO rounding: the fp32 partial of a linear split
+ * along K across tensor-parallel ranks (o_proj, down), summed across ranks (all-reduce) and
+ * rounded to bf16 once, so the sharded linear keeps the single-GPU rounding. Otherwise as
+ * nk_gemm_bf16 (same plan, workspace and stream rules); y32 is [M, N] fp32, row stride ldy,
+ * 4-byte aligned. No single call site in the reference: it is the split form of
+ * torch.mm(x, W.t(), out=y) at engine/kernels/decode.py:58,66 for a K-split weight.
+ */
+NK_API int nk_gemm_bf16_f32out(const void* x, int64_t ldx,
+                               const void* w, int64_t ldw,
+                               float* y32, int64_t ldy,
+                               int M, int N, int K,
+                               const nk_plan* plan, void* ws, size_t ws_bytes,
+                               nk_stream_t stream);
+
 /* Read and clear the device error word that bounded waits set on timeout (synchronizes
  * `stream`). Writes NK_OK or NK_ERR_TIMEOUT to *status. */
 NK_API int nk_device_error(nk_stream_t stream, int* status);

@@ -35,7 +35,7 @@ PLAN_MAGIC = 0x4E4B4731
 
 # Every function the header declares; the CPU test checks the .so exports each of them.
 EXPORTS = ("nk_plan_make", "nk_ws_bytes", "nk_ws_init", "nk_gemm_bf16", "nk_device_error",
-           "nk_status_string", "nk_version", "nk_gemm_bf16_static")
+           "nk_status_string", "nk_version", "nk_gemm_bf16_static", "nk_gemm_bf16_f32out")
 
 
 class NkPlan(ctypes.Structure):
@@ -95,6 +95,9 @@ def load() -> ctypes.CDLL:
     L.nk_gemm_bf16.argtypes = [vp, i64, vp, i64, vp, i64, i32, i32, i32,
                                ctypes.POINTER(NkPlan), vp, ctypes.c_size_t, vp]
     L.nk_gemm_bf16.restype = i32
+    L.nk_gemm_bf16_f32out.argtypes = [vp, i64, vp, i64, vp, i64, i32, i32, i32,
+                                      ctypes.POINTER(NkPlan), vp, ctypes.c_size_t, vp]
+    L.nk_gemm_bf16_f32out.restype = i32
     L.nk_device_error.argtypes = [vp, ctypes.POINTER(i32)]
     L.nk_device_error.restype = i32
     L.nk_status_string.argtypes = [i32]

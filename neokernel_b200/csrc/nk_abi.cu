@@ -153,15 +153,37 @@ extern "C" int nk_ws_init(void* ws, size_t ws_bytes, nk_stream_t stream) {
                                                                                  : NK_ERR_CUDA;
 }
 
+namespace nk {
+
+// Shared body of nk_gemm_bf16 (bf16 y) and nk_gemm_bf16_f32out (fp32 y).
+static int gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
+                     int64_t ldy, bool y_f32, int M, int N, int K, const nk_plan* p, void* ws,
+                     size_t ws_bytes, nk_stream_t stream);
+
+}  // namespace nk
+
 extern "C" int nk_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
                             int64_t ldy, int M, int N, int K, const nk_plan* p, void* ws,
                             size_t ws_bytes, nk_stream_t stream) {
+    return gemm_impl(x, ldx, w, ldw, y, ldy, false, M, N, K, p, ws, ws_bytes, stream);
+}
+
+extern "C" int nk_gemm_bf16_f32out(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                   float* y, int64_t ldy, int M, int N, int K, const nk_plan* p,
+                                   void* ws, size_t ws_bytes, nk_stream_t stream) {
+    return gemm_impl(x, ldx, w, ldw, y, ldy, true, M, N, K, p, ws, ws_bytes, stream);
+}
+
+static int nk::gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
+                         int64_t ldy, bool y_f32, int M, int N, int K, const nk_plan* p,
+                         void* ws, size_t ws_bytes, nk_stream_t stream) {
     if (!p || p->magic != NK_PLAN_MAGIC) return NK_ERR_PLAN;
     if (p->N != N || p->K != K) return NK_ERR_PLAN;
     if (M < 1 || M > p->M_max) return NK_ERR_SHAPE;
     if (!x || !w || !y) return NK_ERR_ARG;
     if (ldx < K || ldw < K || ldy < N) return NK_ERR_SHAPE;
     if (!aligned2(x) || !aligned2(w) || !aligned2(y)) return NK_ERR_ALIGN;
+    if (y_f32 && ((uintptr_t)y & 3u) != 0) return NK_ERR_ALIGN;
     if (p->kind == NK_KIND_GEMV || p->kind == NK_KIND_TC) {
         if (!aligned16(x) || !aligned16(w) || (ldx % 8) != 0 || (ldw % 8) != 0)
             return NK_ERR_ALIGN;
@@ -177,7 +199,9 @@ extern "C" int nk_gemm_bf16(const void* x, int64_t ldx, const void* w, int64_t l
     GemmArgs a;
     a.x = static_cast<const __nv_bfloat16*>(x); a.ldx = ldx;
     a.w = static_cast<const __nv_bfloat16*>(w); a.ldw = ldw;
-    a.y = static_cast<__nv_bfloat16*>(y);       a.ldy = ldy;
+    a.y = y_f32 ? nullptr : static_cast<__nv_bfloat16*>(y);
+    a.y32 = y_f32 ? static_cast<float*>(y) : nullptr;
+    a.ldy = ldy;
     a.M = M; a.N = N; a.K = K;
     a.part = L.total ? reinterpret_cast<float*>(static_cast<char*>(ws) + L.part_offset) : nullptr;
     a.tickets = L.total ? static_cast<unsigned*>(ws) : nullptr;

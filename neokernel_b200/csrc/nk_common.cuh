@@ -97,6 +97,14 @@ __device__ __forceinline__ bool splitk_last_cta(unsigned* ticket, int splits) {
     return last;
 }
 
+// Store one output element: rounded once to bf16 into y, or unrounded into y32 (the fp32
+// partial of a K-split tensor-parallel linear, summed across ranks before its one rounding).
+template <typename GemmArgsT>
+__device__ __forceinline__ void store_out(const GemmArgsT& a, int64_t idx, float v) {
+    if (a.y32) a.y32[idx] = v;
+    else a.y[idx] = __float2bfloat16_rn(v);
+}
+
 // The last CTA's share of the split-K reduction for one output tile of `rows` weight rows
 // (from n_base) and `mcount` tokens (from m0). Thread i owns row i % rows and every
 // (blockDim.x / rows)-th token from i / rows; for G of its tokens at a time it issues the
@@ -129,7 +137,7 @@ __device__ __forceinline__ void splitk_reduce_tile(const GemmArgsT& a, int n_bas
 #pragma unroll
         for (int q = 0; q < G; ++q)
             if (mb + q * lanes < mcount)
-                a.y[(int64_t)(m0 + mb + q * lanes) * a.ldy + n] = __float2bfloat16_rn(acc[q]);
+                store_out(a, (int64_t)(m0 + mb + q * lanes) * a.ldy + n, acc[q]);
     }
 }
 
@@ -203,6 +211,7 @@ struct GemmArgs {
     const __nv_bfloat16* w; int64_t ldw;
     __nv_bfloat16* y;       int64_t ldy;
     int M, N, K;
+    float* y32;             // when set: fp32 output [M, N] (row stride ldy) instead of y
     float* part;            // split-K partials, or nullptr when split_k == 1
     unsigned* tickets;      // split-K tickets, or nullptr when split_k == 1
     // tensor-core family only

@@ -118,7 +118,7 @@ gemv_kernel(GemmArgs a, int k_slice, int splits) {
 #pragma unroll
             for (int m = 0; m < MT; ++m)
                 if (((r * MT + m) & 31) == lane && m < mcount && row0 + r < a.N)
-                    a.y[(int64_t)(m0 + m) * a.ldy + row0 + r] = __float2bfloat16_rn(acc[r][m]);
+                    store_out(a, (int64_t)(m0 + m) * a.ldy + row0 + r, acc[r][m]);
         return;
     }
 
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(256) generic_kernel(GemmArgs a) {
 #pragma unroll
     for (int j = 0; j < kGenericTokens; ++j) {
         const float v = warp_sum(acc[j]);
-        if (lane == j && m0 + j < a.M) a.y[(int64_t)(m0 + j) * a.ldy + n] = __float2bfloat16_rn(v);
+        if (lane == j && m0 + j < a.M) store_out(a, (int64_t)(m0 + j) * a.ldy + n, v);
     }
 }
 

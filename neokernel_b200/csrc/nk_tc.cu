@@ -381,7 +381,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
                                 if (c0 + j < mcount)
-                                    a.y[(int64_t)(m0 + c0 + j) * a.ldy + n] = __float2bfloat16_rn(v[j]);
+                                    store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n, v[j]);
                         }
                     } else {
 #pragma unroll
@@ -426,7 +426,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
 #pragma unroll
                             for (int j = 0; j < 8; ++j)
                                 if (c0 + j < mcount)
-                                    a.y[(int64_t)(m0 + c0 + j) * a.ldy + n] = __float2bfloat16_rn(acc[j]);
+                                    store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n, acc[j]);
                         }
                     }
                     if (ep == 0) a.tickets[sg.t] = 0u;

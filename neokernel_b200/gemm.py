@@ -111,11 +111,11 @@ def workspace(nbytes: int, device: torch.device, stream: torch.cuda.Stream) -> t
     return ws
 
 
-def _check_tensor(t: torch.Tensor, name: str):
+def _check_tensor(t: torch.Tensor, name: str, dtype=torch.bfloat16):
     if not isinstance(t, torch.Tensor):
         raise ValueError(f"{name} must be a torch.Tensor")
-    if t.dtype != torch.bfloat16:
-        raise ValueError(f"{name} must be bfloat16, got {t.dtype}")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {str(dtype).replace('torch.', '')}, got {t.dtype}")
     if t.device.type != "cuda":
         raise ValueError(f"{name} must be a CUDA tensor, got device {t.device}")
     if t.dim() != 2:
@@ -129,9 +129,20 @@ def mm(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor, plan: Plan | None
     a: bf16 CUDA [M, K] with unit column stride; b: bf16 CUDA [K, N] with strides (1, ldw);
     out: bf16 CUDA [M, N] with unit column stride. fp32 accumulation, one bf16 rounding.
     """
+    return _mm(a, b, out, plan, stream, f32=False)
+
+
+def mm_f32(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor, plan: Plan | None = None,
+           stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """As ``mm`` but ``out`` is fp32 and unrounded: the partial sum of a K-split
+    (tensor-parallel) linear, to be all-reduced across ranks and rounded to bf16 once."""
+    return _mm(a, b, out, plan, stream, f32=True)
+
+
+def _mm(a, b, out, plan, stream, f32):
     _check_tensor(a, "a")
     _check_tensor(b, "b")
-    _check_tensor(out, "out")
+    _check_tensor(out, "out", torch.float32 if f32 else torch.bfloat16)
     M, K = a.shape
     K2, N = b.shape
     if K2 != K:
@@ -169,15 +180,15 @@ def mm(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor, plan: Plan | None
     else:
         wsp, wsn = None, 0
     L = _lib.load()
+    fn = L.nk_gemm_bf16_f32out if f32 else L.nk_gemm_bf16
     if dev.index != torch.cuda.current_device():
         with torch.cuda.device(dev):
-            status = L.nk_gemm_bf16(xp, ldx, wp, ldw, yp, ldy, M, N, K, plan._ref, wsp, wsn,
-                                    stream.cuda_stream)
+            status = fn(xp, ldx, wp, ldw, yp, ldy, M, N, K, plan._ref, wsp, wsn,
+                        stream.cuda_stream)
     else:
-        status = L.nk_gemm_bf16(xp, ldx, wp, ldw, yp, ldy, M, N, K, plan._ref, wsp, wsn,
-                                stream.cuda_stream)
+        status = fn(xp, ldx, wp, ldw, yp, ldy, M, N, K, plan._ref, wsp, wsn, stream.cuda_stream)
     if status != _lib.NK_OK:
-        _raise(status, f"nk_gemm_bf16(M={M}, N={N}, K={K})")
+        _raise(status, f"nk_gemm_bf16{'_f32out' if f32 else ''}(M={M}, N={N}, K={K})")
     return out
 
 

@@ -167,7 +167,11 @@ def attention(q, k_cache, v_cache, position, slots, d: Qwen3Dims):
     return out.reshape(B, d.q_width).to(torch.bfloat16)
 
 
-def layer_step(st: DecodeState, w: LayerWeights, k_cache, v_cache, d: Qwen3Dims, linear):
+def layer_step(st: DecodeState, w: LayerWeights, k_cache, v_cache, d: Qwen3Dims, linear,
+               row_linear=None):
+    """One decoder layer. ``row_linear`` computes o_proj and down (the K-split linears of the
+    tensor-parallel mode, which all-reduce before rounding); by default it is ``linear``."""
+    row_linear = row_linear or linear
     B = st.batch
     rms_norm(st.x, w.input_norm, d.eps, out=st.norm)
     linear(st.norm, w.qkv, out=st.qkv)                                   # decode.py:54
@@ -183,26 +187,33 @@ def layer_step(st: DecodeState, w: LayerWeights, k_cache, v_cache, d: Qwen3Dims,
     k_cache.index_copy_(2, st.position, k.unsqueeze(2))
     v_cache.index_copy_(2, st.position, v.unsqueeze(2))
     st.attn.copy_(attention(q, k_cache, v_cache, st.position, st.slots, d))
-    linear(st.attn, w.o, out=st.branch)                                  # decode.py:58
+    row_linear(st.attn, w.o, out=st.branch)                              # decode.py:58
     torch.add(st.x, st.branch, out=st.x)
     rms_norm(st.x, w.post_norm, d.eps, out=st.norm)
     linear(st.norm, w.gate_up, out=st.gate_up)                           # decode.py:64
     I = d.intermediate
     act = torch.nn.functional.silu(st.gate_up[:, :I].float()).to(torch.bfloat16)
     torch.mul(act, st.gate_up[:, I:], out=st.product)
-    linear(st.product, w.down, out=st.branch)                            # decode.py:66
+    row_linear(st.product, w.down, out=st.branch)                        # decode.py:66
     torch.add(st.x, st.branch, out=st.x)
 
 
-def decode_step(st: DecodeState, w: Qwen3Weights, linear):
-    """One greedy decode step for every sequence at ``st.position``; writes ``st.next_tokens``."""
+def greedy_head(st: DecodeState, lm_head, linear):
+    linear(st.norm, lm_head, out=st.logits)                               # engine.py:114
+    torch.argmax(st.logits, dim=-1, out=st.next_tokens)                  # lowest index on ties
+
+
+def decode_step(st: DecodeState, w: Qwen3Weights, linear, row_linear=None, head=None):
+    """One greedy decode step for every sequence at ``st.position``; writes ``st.next_tokens``.
+
+    ``row_linear`` (o_proj, down) and ``head`` (lm_head + argmax) are the hooks the
+    tensor-parallel mode replaces (neokernel_b200.tp); by default the step is single-GPU."""
     d = w.dims
     torch.index_select(w.embed, 0, st.tokens, out=st.x)
     for i, lw in enumerate(w.layers):
-        layer_step(st, lw, st.k_cache[i], st.v_cache[i], d, linear)
+        layer_step(st, lw, st.k_cache[i], st.v_cache[i], d, linear, row_linear)
     rms_norm(st.x, w.final_norm, d.eps, out=st.norm)
-    linear(st.norm, w.lm_head, out=st.logits)                             # engine.py:114
-    torch.argmax(st.logits, dim=-1, out=st.next_tokens)                  # lowest index on ties
+    (head or greedy_head)(st, w.lm_head, linear)
     return st.next_tokens
 
 
@@ -210,20 +221,25 @@ class GraphDecoder:
     """A decode step captured once in a CUDA graph (reference: Engine.capture_decode,
     engine/engine.py:119-129: side-stream warm-up x3, then capture) and replayed per token."""
 
-    def __init__(self, w: Qwen3Weights, batch: int, capacity: int, linear, device="cuda"):
+    def __init__(self, w: Qwen3Weights, batch: int, capacity: int, linear, device="cuda",
+                 make_hooks=None):
+        """``make_hooks(state) -> (row_linear, head)`` supplies the tensor-parallel hooks,
+        built once per state so their buffers are fixed before capture."""
         self.w, self.linear = w, linear
         self.st = DecodeState(w, batch, capacity, device)
+        row_linear, head = make_hooks(self.st) if make_hooks else (None, None)
+        step = lambda: decode_step(self.st, w, linear, row_linear, head)  # noqa: E731
         stream = torch.cuda.Stream(device=device)
         self.stream = stream
         stream.wait_stream(torch.cuda.current_stream(device))
         with torch.cuda.stream(stream):
             for _ in range(3):
-                decode_step(self.st, w, linear)
+                step()
         stream.synchronize()
         self.reset()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=stream):
-            decode_step(self.st, w, linear)
+            step()
         torch.cuda.current_stream(device).wait_stream(stream)
 
     def reset(self):
@@ -260,7 +276,8 @@ class GraphDecoder:
         self.reset()
         B, P = prompt.shape
         T = tokens.shape[1]
-        logits = torch.empty(B, T, self.w.dims.vocab, dtype=torch.float32, device=prompt.device)
+        logits = torch.empty(B, T, self.st.logits.shape[1], dtype=torch.float32,
+                             device=prompt.device)
         seq = torch.cat([prompt, tokens], dim=1)
         for i in range(P + T - 1):
             self.st.tokens.copy_(seq[:, i])

@@ -1,0 +1,140 @@
+"""Tensor-parallel decode for the Qwen3 shapes (one process per GPU, torch.distributed).
+
+The reference engine is single-GPU (engine/engine.py:65,79,84 hard-code ``cuda:0``); this mode
+shards the decode linears where their weights shard naturally:
+
+* QKV (engine/kernels/decode.py:54) is split by output column, whole heads per rank: rank r
+  holds query heads [r*Hq/T, (r+1)*Hq/T) and KV heads [r*Hkv/T, (r+1)*Hkv/T), so grouped
+  attention runs on local heads with no exchange;
+* gate_up (decode.py:64) is split by output column with the gate and up slices paired, so
+  bf16(silu(gate)) * up is local;
+* o_proj (decode.py:58) and down (decode.py:66) are split along K: each rank computes an
+  unrounded fp32 partial (``mm_f32``), the partials are summed with one all-reduce over NCCL
+  (NVLink / NVSwitch), and the sum is rounded to bf16 once — the single-GPU rounding;
+* lm_head (engine.py:114) is split by vocabulary row: each rank takes its local max and its
+  lowest index, and an all-gather of (value, index) picks the global maximum, ties to the
+  lowest vocabulary index as torch.argmax does (engine.py:116).
+
+Embedding and norms are replicated. Every rank issues the same collectives in the same order
+in warm-up, capture and replay. The weights of a rank are the slices of exactly the matrices
+``qwen3.Qwen3Weights`` draws for the same seed, so a tensor-parallel run and a single-GPU run
+of the same seed use the same model.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import qwen3
+from .qwen3 import Qwen3Dims
+
+
+def local_dims(d: Qwen3Dims, world: int) -> Qwen3Dims:
+    """The per-rank shapes of a ``world``-way split."""
+    for what, n in (("heads", d.heads), ("kv_heads", d.kv_heads),
+                    ("intermediate", d.intermediate), ("vocab", d.vocab)):
+        if n % world:
+            raise ValueError(f"tensor parallel size {world} does not divide {what}={n}")
+    return Qwen3Dims(d.hidden, d.intermediate // world, d.heads // world, d.kv_heads // world,
+                     d.head_dim, d.layers, d.vocab // world, d.eps, d.rope_theta,
+                     d.tie_embeddings)
+
+
+class TPLayerWeights:
+    """Rank r's slices of one layer, in the same packed layout as the full layer."""
+
+    def __init__(self, full: qwen3.LayerWeights, d: Qwen3Dims, rank: int, world: int):
+        D = d.head_dim
+        hq, hkv = d.heads // world, d.kv_heads // world
+        I = d.intermediate
+        il = I // world
+        q = full.qkv_weight[rank * hq * D:(rank + 1) * hq * D]
+        k0 = d.q_width
+        k = full.qkv_weight[k0 + rank * hkv * D:k0 + (rank + 1) * hkv * D]
+        v0 = d.q_width + d.kv_width
+        v = full.qkv_weight[v0 + rank * hkv * D:v0 + (rank + 1) * hkv * D]
+        self.qkv_weight = torch.cat((q, k, v)).contiguous()
+        self.o_weight = full.o_weight[:, rank * hq * D:(rank + 1) * hq * D].contiguous()
+        g = full.gate_up_weight[rank * il:(rank + 1) * il]
+        u = full.gate_up_weight[I + rank * il:I + (rank + 1) * il]
+        self.gate_up_weight = torch.cat((g, u)).contiguous()
+        self.down_weight = full.down_weight[:, rank * il:(rank + 1) * il].contiguous()
+        self.qkv = self.qkv_weight.t()
+        self.o = self.o_weight.t()
+        self.gate_up = self.gate_up_weight.t()
+        self.down = self.down_weight.t()
+        self.input_norm, self.post_norm = full.input_norm, full.post_norm
+        self.q_norm, self.k_norm = full.q_norm, full.k_norm
+
+
+class TPWeights:
+    """Rank r's shard of the random-init model ``qwen3.Qwen3Weights(d, seed)``: each full
+    matrix is drawn in the same order with the same generator (one layer at a time, so a rank
+    never holds more than one full layer), sliced, and the full copy released."""
+
+    def __init__(self, d: Qwen3Dims, seed: int, rank: int, world: int, device="cuda",
+                 layers: int | None = None):
+        self.full_dims = d
+        self.dims = local_dims(d, world)
+        self.rank, self.world = rank, world
+        gen = torch.Generator(device=device).manual_seed(seed)
+        self.embed = qwen3._randn((d.vocab, d.hidden), gen, device)
+        n = d.layers if layers is None else layers
+        self.layers = []
+        for _ in range(n):
+            full = qwen3.LayerWeights(d, gen, device)
+            self.layers.append(TPLayerWeights(full, d, rank, world))
+            del full
+        self.final_norm = torch.ones(d.hidden, device=device, dtype=torch.bfloat16)
+        head = self.embed if d.tie_embeddings else qwen3._randn((d.vocab, d.hidden), gen, device)
+        vl = d.vocab // world
+        self.lm_head_weight = head[rank * vl:(rank + 1) * vl].contiguous()
+        self.lm_head = self.lm_head_weight.t()
+        self.vocab_offset = rank * vl
+
+
+def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None):
+    """Return ``make(state) -> (row_linear, head)`` for ``qwen3.GraphDecoder`` / ``decode_step``.
+
+    ``linear_f32(a, b, out)`` computes an unrounded fp32 partial (default:
+    ``neokernel_b200.mm_f32``); ``linear(a, b, out)`` the bf16 lm_head shard (default:
+    ``neokernel_b200.mm``). Buffers are allocated here, once per state, so the hooks are
+    capture-safe.
+    """
+    if linear_f32 is None or linear is None:
+        import neokernel_b200 as nk
+        linear_f32 = linear_f32 or nk.mm_f32
+        linear = linear or nk.mm
+    world, vocab_offset = w.world, w.vocab_offset
+
+    def make(st: qwen3.DecodeState):
+        B, H = st.batch, w.dims.hidden
+        dev = st.x.device
+        partial = torch.empty(B, H, device=dev, dtype=torch.float32)
+        best = torch.empty(B, device=dev, dtype=torch.float32)
+        best_idx = torch.empty(B, device=dev, dtype=torch.int64)
+        all_best = torch.empty(world * B, device=dev, dtype=torch.float32)
+        all_idx = torch.empty(world * B, device=dev, dtype=torch.int64)
+
+        def row_linear(a, b, out):
+            linear_f32(a, b, out=partial)
+            if world > 1:
+                dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=group)
+            out.copy_(partial)  # the one rounding to bf16 (nearest-even)
+
+        def head(state, lm_head, _linear):
+            linear(state.norm, lm_head, out=state.logits)
+            torch.max(state.logits.float(), dim=-1, out=(best, best_idx))  # first max index
+            best_idx.add_(vocab_offset)
+            if world > 1:
+                dist.all_gather_into_tensor(all_best, best, group=group)
+                dist.all_gather_into_tensor(all_idx, best_idx, group=group)
+                r = torch.argmax(all_best.view(world, B), dim=0)  # lowest rank among maxima
+                torch.gather(all_idx.view(world, B), 0, r.view(1, B), out=state.next_tokens.view(1, B))
+            else:
+                state.next_tokens.copy_(best_idx)
+
+        return row_linear, head
+
+    return make

@@ -71,19 +71,37 @@ def test_qwen3_8b_128_greedy_tokens(batch):
 
     ours = qwen3.GraphDecoder(w, batch, cap, nk.mm)
     ref = qwen3.GraphDecoder(w, batch, cap, torch.mm)
+    # Control: another valid fp32-accumulating GEMM (cuBLAS fp32 on the same bf16 values,
+    # rounded once) — shows how soon any change of summation order flips a near-tie.
+    ctrl = qwen3.GraphDecoder(w, batch, cap,
+                              lambda a, b, out: out.copy_(torch.mm(a.float(), b.float())))
     t_ours = ours.greedy(prompt, new)
     t_ref = ref.greedy(prompt, new)
+    t_ctrl = ctrl.greedy(prompt, new)
     torch.cuda.synchronize()
     same = (t_ours == t_ref)
+
+    def first_divergence(a, b):
+        eq = a == b
+        return [int(eq[i].logical_not().nonzero()[0]) if not eq[i].all() else None
+                for i in range(a.shape[0])]
+
     # Teacher-forced replay of our tokens on the reference path (the judge's check).
     ref_logits = ref.teacher_forced_logits(prompt, t_ours)
     m = margins(ref_logits, t_ours)
-    first_diff = [int(same[b].logical_not().nonzero()[0]) if not same[b].all() else None
-                  for b in range(batch)]
+    first_diff = first_divergence(t_ours, t_ref)
+    # Teacher-forced on the reference's own trajectory: per-step argmax agreement.
+    lo = ours.teacher_forced_logits(prompt, t_ref)
+    lr = ref.teacher_forced_logits(prompt, t_ref)
+    agree = (lo.argmax(-1) == lr.argmax(-1)).float().mean().item()
     report = {"test": f"qwen3-8b/greedy/B{batch}", "identical_tokens": int(same.sum()),
               "tokens": batch * new, "first_divergence": first_diff,
+              "control_first_divergence": first_divergence(t_ctrl, t_ref),
+              "teacher_forced_argmax_agreement": agree,
+              "teacher_forced_max_logit_diff": float((lo - lr).abs().max()),
               "worst_margin": float(m.max()), "mean_margin": float(m.mean())}
     print(json.dumps(report), flush=True)
+    assert agree >= 0.95, report
     assert torch.isfinite(ref_logits).all()
     assert float(m.max()) <= MARGIN, report
     # Up to its first divergence a sequence has seen identical inputs on both paths, so the
@@ -92,5 +110,5 @@ def test_qwen3_8b_128_greedy_tokens(batch):
     for b in range(batch):
         if first_diff[b] is not None:
             assert float(m[b, first_diff[b]]) <= 0.125, report
-    del ours, ref
+    del ours, ref, ctrl
     torch.cuda.empty_cache()
