@@ -29,7 +29,7 @@
 //
 // Every mbarrier wait is bounded: on expiry the thread records NK_ERR_TIMEOUT in the device
 // error word and the CTA stops storing, drains its outstanding copies and MMAs (bounded),
-// frees its TMEM and exits. No TMA multicast is used anywhere.
+// frees its TMEM and exits. Every TMA load here fills only the issuing CTA's own shared memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
