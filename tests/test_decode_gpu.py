@@ -90,18 +90,26 @@ def test_qwen3_8b_128_greedy_tokens(batch):
     ref_logits = ref.teacher_forced_logits(prompt, t_ours)
     m = margins(ref_logits, t_ours)
     first_diff = first_divergence(t_ours, t_ref)
-    # Teacher-forced on the reference's own trajectory: per-step argmax agreement.
+    # Teacher-forced on the reference's own trajectory: per-step argmax agreement with the
+    # reference, for our kernels and for the control GEMM.
     lo = ours.teacher_forced_logits(prompt, t_ref)
     lr = ref.teacher_forced_logits(prompt, t_ref)
+    lc = ctrl.teacher_forced_logits(prompt, t_ref)
     agree = (lo.argmax(-1) == lr.argmax(-1)).float().mean().item()
+    agree_ctrl = (lc.argmax(-1) == lr.argmax(-1)).float().mean().item()
     report = {"test": f"qwen3-8b/greedy/B{batch}", "identical_tokens": int(same.sum()),
               "tokens": batch * new, "first_divergence": first_diff,
               "control_first_divergence": first_divergence(t_ctrl, t_ref),
               "teacher_forced_argmax_agreement": agree,
+              "control_teacher_forced_argmax_agreement": agree_ctrl,
               "teacher_forced_max_logit_diff": float((lo - lr).abs().max()),
+              "control_teacher_forced_max_logit_diff": float((lc - lr).abs().max()),
               "worst_margin": float(m.max()), "mean_margin": float(m.mean())}
     print(json.dumps(report), flush=True)
-    assert agree >= 0.95, report
+    # Our kernels agree with the reference's own GEMM as well as another valid
+    # fp32-accumulating GEMM does (a few percent of slack for the 128-sample noise).
+    assert agree >= agree_ctrl - 0.05, report
+    assert float((lo - lr).abs().max()) <= 2 * float((lc - lr).abs().max()) + 0.0625, report
     assert torch.isfinite(ref_logits).all()
     assert float(m.max()) <= MARGIN, report
     # Up to its first divergence a sequence has seen identical inputs on both paths, so the
