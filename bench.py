@@ -468,16 +468,20 @@ def single(args):
 
 def decode_bench(nk, dev, batches, world, local, kv=1024, steps=20, warmup=3):
     """Decode tokens/s of the full Qwen3-8B step (36 layers, random init, CUDA graph) at KV
-    length 1024, with the decode linears on neokernel_b200.mm and, for comparison in the same
-    harness, on torch.mm (cuBLAS, the reference's call). Non-linear ops are PyTorch in both."""
+    length 1024. Arms: the product (fused non-linear kernels + neokernel_b200.mm), the same
+    fused step with the linears on torch.mm (cuBLAS, the reference's call), and the step with
+    PyTorch non-linear ops and torch.mm."""
     from neokernel_b200 import qwen3
     w = qwen3.Qwen3Weights(qwen3.QWEN3_8B, seed=7, device=dev)
     out = {"model": "qwen3-8b random-init, 36 layers, vocab 151936", "kv_length": kv,
            "steps": steps, "timing": "CUDA events around graph replays, max over ranks"}
-    for name, linear in (("neokernel_b200", nk.mm), ("torch_mm", torch.mm)):
+    arms = (("neokernel_b200", nk.mm, True), ("fused_ops_torch_mm", torch.mm, True),
+            ("torch_ops_torch_mm", torch.mm, False))
+    for name, linear, fused in arms:
         res = {}
         for B in batches:
-            g = qwen3.GraphDecoder(w, B, kv + warmup + steps + 1, linear, device=dev)
+            g = qwen3.GraphDecoder(w, B, kv + warmup + steps + 1, linear, device=dev,
+                                   fused=fused)
             gen = torch.Generator(device=dev).manual_seed(B)
             for c in g.st.k_cache + g.st.v_cache:
                 c.normal_(generator=gen)
@@ -515,7 +519,7 @@ def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, war
     res = {}
     for B in batches:
         g = qwen3.GraphDecoder(w, B, kv + warmup + steps + 1, nk.mm, device=dev,
-                               make_hooks=tp.make_hooks(w))
+                               make_hooks=tp.make_hooks(w), fused=True)
         gen = torch.Generator(device=dev).manual_seed(100 + B)
         for c in g.st.k_cache + g.st.v_cache:
             c.normal_(generator=gen)

@@ -35,7 +35,9 @@ PLAN_MAGIC = 0x4E4B4731
 
 # Every function the header declares; the CPU test checks the .so exports each of them.
 EXPORTS = ("nk_plan_make", "nk_ws_bytes", "nk_ws_init", "nk_gemm_bf16", "nk_device_error",
-           "nk_status_string", "nk_version", "nk_gemm_bf16_static", "nk_gemm_bf16_f32out")
+           "nk_status_string", "nk_version", "nk_gemm_bf16_static", "nk_gemm_bf16_f32out",
+           "nk_rmsnorm_bf16", "nk_qk_norm_rope_cache_bf16", "nk_attention_ws_bytes",
+           "nk_attention_decode_bf16", "nk_silu_mul_bf16")
 
 
 class NkPlan(ctypes.Structure):
@@ -98,6 +100,19 @@ def load() -> ctypes.CDLL:
     L.nk_gemm_bf16_f32out.argtypes = [vp, i64, vp, i64, vp, i64, i32, i32, i32,
                                       ctypes.POINTER(NkPlan), vp, ctypes.c_size_t, vp]
     L.nk_gemm_bf16_f32out.restype = i32
+    f32 = ctypes.c_float
+    L.nk_rmsnorm_bf16.argtypes = [vp, vp, vp, vp, i32, i32, f32, vp]
+    L.nk_rmsnorm_bf16.restype = i32
+    L.nk_qk_norm_rope_cache_bf16.argtypes = [vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32,
+                                             i32, i32, i64, i64, i64, f32, vp]
+    L.nk_qk_norm_rope_cache_bf16.restype = i32
+    L.nk_attention_ws_bytes.argtypes = [i32, i32, i32]
+    L.nk_attention_ws_bytes.restype = ctypes.c_size_t
+    L.nk_attention_decode_bf16.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i64, i64,
+                                           i64, f32, vp, ctypes.c_size_t, vp]
+    L.nk_attention_decode_bf16.restype = i32
+    L.nk_silu_mul_bf16.argtypes = [vp, vp, i32, i32, vp]
+    L.nk_silu_mul_bf16.restype = i32
     L.nk_device_error.argtypes = [vp, ctypes.POINTER(i32)]
     L.nk_device_error.restype = i32
     L.nk_status_string.argtypes = [i32]

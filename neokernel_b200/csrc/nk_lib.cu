@@ -5,3 +5,4 @@
 #include "nk_tc.cu"
 #include "nk_abi.cu"
 #include "nk_static.cu"
+#include "nk_decode.cu"

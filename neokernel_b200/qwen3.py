@@ -153,6 +153,8 @@ class DecodeState:
         self.v_cache = [torch.zeros(batch, d.kv_heads, capacity, d.head_dim, **bf) for _ in range(n)]
         self.cos, self.sin = rope_tables(d, capacity, device)
         self.slots = torch.arange(capacity, device=device)
+        self.q = torch.empty(batch, d.q_width, **bf)
+        self.attn_ws = None  # fused path: split-KV partials, made on first fused step
 
 
 def attention(q, k_cache, v_cache, position, slots, d: Qwen3Dims):
@@ -192,10 +194,31 @@ def layer_step(st: DecodeState, w: LayerWeights, k_cache, v_cache, d: Qwen3Dims,
     rms_norm(st.x, w.post_norm, d.eps, out=st.norm)
     linear(st.norm, w.gate_up, out=st.gate_up)                           # decode.py:64
     I = d.intermediate
-    act = torch.nn.functional.silu(st.gate_up[:, :I].float()).to(torch.bfloat16)
+    g = st.gate_up[:, :I].float()
+    act = (g / (1.0 + torch.exp(-g))).to(torch.bfloat16)   # elementwise.py:86
     torch.mul(act, st.gate_up[:, I:], out=st.product)
     row_linear(st.product, w.down, out=st.branch)                        # decode.py:66
     torch.add(st.x, st.branch, out=st.x)
+
+
+def layer_step_fused(st: DecodeState, w: LayerWeights, k_cache, v_cache, d: Qwen3Dims, linear,
+                     row_linear=None, carry=False):
+    """The same layer on the fused kernels (neokernel_b200.decode_ops), with the reference's
+    fuse_norm_residual scheme (engine/kernels/decode.py:42-68): the down projection's output
+    stays in ``branch`` and the next RMSNorm adds it into ``x`` (``carry``)."""
+    from . import decode_ops as ops
+    row_linear = row_linear or linear
+    ops.rmsnorm(st.x, w.input_norm, st.norm, d.eps, branch=st.branch if carry else None)
+    linear(st.norm, w.qkv, out=st.qkv)                                   # decode.py:54
+    ops.qk_norm_rope_cache(st.qkv, w.q_norm, w.k_norm, st.cos, st.sin, st.position, st.q,
+                           k_cache, v_cache, d.heads, d.kv_heads, d.eps)
+    ops.attention_decode(st.q, k_cache, v_cache, st.position, st.attn, st.attn_ws,
+                         d.heads, d.kv_heads)
+    row_linear(st.attn, w.o, out=st.branch)                              # decode.py:58
+    ops.rmsnorm(st.x, w.post_norm, st.norm, d.eps, branch=st.branch)
+    linear(st.norm, w.gate_up, out=st.gate_up)                           # decode.py:64
+    ops.silu_mul(st.gate_up, st.product)
+    row_linear(st.product, w.down, out=st.branch)                        # decode.py:66
 
 
 def greedy_head(st: DecodeState, lm_head, linear):
@@ -203,16 +226,28 @@ def greedy_head(st: DecodeState, lm_head, linear):
     torch.argmax(st.logits, dim=-1, out=st.next_tokens)                  # lowest index on ties
 
 
-def decode_step(st: DecodeState, w: Qwen3Weights, linear, row_linear=None, head=None):
+def decode_step(st: DecodeState, w: Qwen3Weights, linear, row_linear=None, head=None,
+                fused=False):
     """One greedy decode step for every sequence at ``st.position``; writes ``st.next_tokens``.
 
     ``row_linear`` (o_proj, down) and ``head`` (lm_head + argmax) are the hooks the
-    tensor-parallel mode replaces (neokernel_b200.tp); by default the step is single-GPU."""
+    tensor-parallel mode replaces (neokernel_b200.tp); by default the step is single-GPU.
+    ``fused`` runs the non-linear ops on the fused CUDA kernels instead of PyTorch ops."""
     d = w.dims
     torch.index_select(w.embed, 0, st.tokens, out=st.x)
-    for i, lw in enumerate(w.layers):
-        layer_step(st, lw, st.k_cache[i], st.v_cache[i], d, linear, row_linear)
-    rms_norm(st.x, w.final_norm, d.eps, out=st.norm)
+    if fused:
+        from . import decode_ops as ops
+        if st.attn_ws is None:
+            st.attn_ws = ops.attention_workspace(st.batch, d.heads, st.capacity, st.x.device)
+        for i, lw in enumerate(w.layers):
+            layer_step_fused(st, lw, st.k_cache[i], st.v_cache[i], d, linear, row_linear,
+                             carry=i > 0)
+        ops.rmsnorm(st.x, w.final_norm, st.norm, d.eps,
+                    branch=st.branch if w.layers else None)
+    else:
+        for i, lw in enumerate(w.layers):
+            layer_step(st, lw, st.k_cache[i], st.v_cache[i], d, linear, row_linear)
+        rms_norm(st.x, w.final_norm, d.eps, out=st.norm)
     (head or greedy_head)(st, w.lm_head, linear)
     return st.next_tokens
 
@@ -222,13 +257,14 @@ class GraphDecoder:
     engine/engine.py:119-129: side-stream warm-up x3, then capture) and replayed per token."""
 
     def __init__(self, w: Qwen3Weights, batch: int, capacity: int, linear, device="cuda",
-                 make_hooks=None):
+                 make_hooks=None, fused=False):
         """``make_hooks(state) -> (row_linear, head)`` supplies the tensor-parallel hooks,
-        built once per state so their buffers are fixed before capture."""
+        built once per state so their buffers are fixed before capture; ``fused`` selects the
+        fused CUDA kernels for the non-linear ops."""
         self.w, self.linear = w, linear
         self.st = DecodeState(w, batch, capacity, device)
         row_linear, head = make_hooks(self.st) if make_hooks else (None, None)
-        step = lambda: decode_step(self.st, w, linear, row_linear, head)  # noqa: E731
+        step = lambda: decode_step(self.st, w, linear, row_linear, head, fused)  # noqa: E731
         stream = torch.cuda.Stream(device=device)
         self.stream = stream
         stream.wait_stream(torch.cuda.current_stream(device))
