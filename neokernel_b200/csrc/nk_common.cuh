@@ -218,6 +218,7 @@ struct GemmArgs {
     int n_tiles;            // ceil(N / 128)
     int segments;           // partial slots per tile
     int part_cols;          // token columns per partial slot (min(NT, M_max))
+    int coresident;         // 1: every CTA of the grid is resident at once (see nk_tc.cu)
     TcPartition part_map;
 };
 

@@ -134,6 +134,27 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait until *count >= target (another CTA of this grid increments it after
+// publishing). Gives up after ~2 s, recording NK_ERR_TIMEOUT; returns whether it was reached.
+__device__ __forceinline__ bool spin_until_count(const unsigned* count, unsigned target) {
+    const volatile unsigned* c = count;
+    const uint64_t t0 = global_ns();
+    while (*c < target) {
+        if (global_ns() - t0 > 2000000000ull) {
+            atomicExch(&g_error, NK_ERR_TIMEOUT);
+            return false;
+        }
+        __nanosleep(64);
+    }
+    return true;
+}
+
 __device__ __forceinline__ void epi_bar() {  // named barrier over the 4 epilogue warps
     asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiThreads) : "memory");
 }
@@ -202,8 +223,11 @@ __device__ __forceinline__ Segment segment_at(int64_t u, int64_t u_end, int KB) 
     return sg;
 }
 
+// Every CTA of the grid must be resident at once (rank-0 CTAs of shared tiles wait for
+// higher CTAs), so the register budget must allow TcSmem<NT>::kPerSm CTAs per SM, and the
+// launch caps the grid by the occupancy the runtime reports.
 template <int NT>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, TcSmem<NT>::kPerSm)
 tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
           GemmArgs a) {
     using L = TcSmem<NT>;
@@ -368,37 +392,84 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                             *abort_flag == 0u;
             tc_fence_after();
             const uint32_t taddr = tmem + (uint32_t)(buf * NT) + tlane;
-            const int rank = c - P.first_cta(sg.t);
-            float* dst = a.part + (((size_t)sg.t * a.segments + rank) * a.part_cols) * kTcRows + row;
-            if (ok) {
+            const int first = P.first_cta(sg.t);
+            const int rank = c - first;
+            const int nseg = whole ? 1 : P.last_cta(sg.t) - first + 1;
+            float* slot0 = a.part + ((size_t)sg.t * a.segments * a.part_cols) * kTcRows + row;
+            const bool wait_mode = a.coresident != 0;
+            if (whole || rank > 0 || !wait_mode) {
+                // Whole tile: bf16 out. Rank >= 1 of a shared tile (always this CTA's first
+                // segment): publish the fp32 partial for the tile's rank-0 CTA. Without a
+                // co-resident grid every rank publishes and the last to arrive sums them.
+                float* dst = slot0 + (size_t)rank * a.part_cols * kTcRows;
+                if (ok) {
 #pragma unroll 1
-                for (int c0 = 0; c0 < NT; c0 += 16) {
-                    if (c0 >= mcount) break;  // warp-uniform
-                    float v[16];
-                    tmem_ld16(taddr + c0, v);
-                    if (whole) {
+                    for (int c0 = 0; c0 < NT; c0 += 16) {
+                        if (c0 >= mcount) break;  // warp-uniform
+                        float v[16];
+                        tmem_ld16(taddr + c0, v);
+                        if (whole) {
+                            if (n < a.N) {
+#pragma unroll
+                                for (int j = 0; j < 16; ++j)
+                                    if (c0 + j < mcount)
+                                        store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n, v[j]);
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                if (c0 + j < mcount) dst[(size_t)(c0 + j) * kTcRows] = v[j];
+                        }
+                    }
+                }
+            } else {
+                // Rank 0 of a shared tile: it holds the tile's first K blocks and this is its
+                // last segment, so the other ranks (higher CTAs, whose share is their first
+                // segment) have published long ago. Wait (bounded) for their count, then sum
+                // own + rank 1 + rank 2 ... — ascending k, the same order whoever is late.
+                if (ep == 0) {
+                    *last_flag = spin_until_count(a.tickets + sg.t, (unsigned)(nseg - 1)) ? 1u : 0u;
+                }
+                epi_bar();
+                __threadfence();
+                if (ok && *last_flag) {
+#pragma unroll 1
+                    for (int c0 = 0; c0 < NT; c0 += 16) {
+                        if (c0 >= mcount) break;  // warp-uniform
+                        float v[16];
+                        tmem_ld16(taddr + c0, v);
+#pragma unroll 4
+                        for (int r = 1; r < nseg; ++r) {
+                            const float* pr = slot0 + ((size_t)r * a.part_cols + c0) * kTcRows;
+                            float p[16];
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                p[j] = (c0 + j < mcount) ? __ldcg(pr + (size_t)j * kTcRows) : 0.f;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) v[j] += p[j];
+                        }
                         if (n < a.N) {
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
                                 if (c0 + j < mcount)
                                     store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n, v[j]);
                         }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            if (c0 + j < mcount) dst[(size_t)(c0 + j) * kTcRows] = v[j];
                     }
                 }
+                if (ep == 0) a.tickets[sg.t] = 0u;  // re-armed for the next launch
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_tempty + 8 * buf);
-            if (!whole) {
-                // Partial segment: the CTA whose arrival completes the tile sums all partials
-                // of the tile in ascending rank (= ascending k) order.
+            if (!whole && wait_mode && rank > 0) {
+                __threadfence();  // this CTA's partial stores, before the count that publishes them
+                epi_bar();
+                if (ep == 0) atomicAdd(a.tickets + sg.t, 1u);
+            } else if (!whole && !wait_mode) {
+                // No waiting: the CTA whose count completes the tile sums every rank's
+                // partial in ascending rank order (the same order as the waiting scheme).
                 __threadfence();
                 epi_bar();
-                const int nseg = P.last_cta(sg.t) - P.first_cta(sg.t) + 1;
                 if (ep == 0) {
                     const unsigned prev = atomicAdd(a.tickets + sg.t, 1u);
                     *last_flag = (prev == (unsigned)(nseg - 1)) ? 1u : 0u;
@@ -406,27 +477,25 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                 epi_bar();
                 if (*last_flag) {
                     __threadfence();
-                    const float* src =
-                        a.part + ((size_t)sg.t * a.segments * a.part_cols) * kTcRows + row;
                     if (n < a.N && *abort_flag == 0u) {
-                        for (int c0 = 0; c0 < mcount; c0 += 8) {
-                            float acc[8];
+                        for (int c0 = 0; c0 < mcount; c0 += 16) {
+                            float v[16];
 #pragma unroll
-                            for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-#pragma unroll 2
+                            for (int j = 0; j < 16; ++j) v[j] = 0.f;
+#pragma unroll 4
                             for (int r = 0; r < nseg; ++r) {
-                                const float* pr = src + ((size_t)r * a.part_cols + c0) * kTcRows;
-                                float v[8];
+                                const float* pr = slot0 + ((size_t)r * a.part_cols + c0) * kTcRows;
+                                float p[16];
 #pragma unroll
-                                for (int j = 0; j < 8; ++j)
-                                    v[j] = (c0 + j < mcount) ? __ldcg(pr + (size_t)j * kTcRows) : 0.f;
+                                for (int j = 0; j < 16; ++j)
+                                    p[j] = (c0 + j < mcount) ? __ldcg(pr + (size_t)j * kTcRows) : 0.f;
 #pragma unroll
-                                for (int j = 0; j < 8; ++j) acc[j] += v[j];
+                                for (int j = 0; j < 16; ++j) v[j] += p[j];
                             }
 #pragma unroll
-                            for (int j = 0; j < 8; ++j)
+                            for (int j = 0; j < 16; ++j)
                                 if (c0 + j < mcount)
-                                    store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n, acc[j]);
+                                    store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n, v[j]);
                         }
                     }
                     if (ep == 0) a.tickets[sg.t] = 0u;
@@ -514,18 +583,44 @@ int tc_ctas_per_sm(int nt) {
 }
 
 template <int NT>
-static int launch_tc_t(int grid, const GemmArgs& a, const CUtensorMap& mw, const CUtensorMap& mx,
-                       cudaStream_t s) {
+static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
+                       const CUtensorMap& mx, cudaStream_t s) {
     using L = TcSmem<NT>;
-    static bool attr_set[64] = {};
+    static int resident[64] = {};  // co-resident CTAs per device (0 = not yet queried)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return NK_ERR_CUDA;
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (dev < 0 || dev >= 64) return NK_ERR_DEVICE;
+    if (resident[dev] == 0) {
         if (cudaFuncSetAttribute(tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 L::kAlloc) != cudaSuccess)
+                                 L::kAlloc) != cudaSuccess ||
+            cudaFuncSetAttribute(tc_kernel<NT>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return NK_ERR_CUDA;
-        attr_set[dev] = true;
+        int per_sm = 0, sms = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tc_kernel<NT>, kTcThreads,
+                                                          L::kAlloc) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return NK_ERR_CUDA;
+        if (per_sm < 1) return NK_ERR_CUDA;
+        resident[dev] = per_sm * sms;
     }
+    TcPartition& P = a.part_map;
+    if (p.split_k > 0) {
+        P.G = (int)(P.U / P.KB) * p.split_k;
+    } else {
+        // Keep at least the plan's units per CTA, so no tile is shared by more CTAs than the
+        // plan's `segments` (the workspace was sized for that); never more CTAs than can be
+        // resident at once.
+        const int64_t U_plan = (int64_t)p.n_tiles * p.m_tiles * P.KB;
+        const int64_t q = U_plan / p.grid;
+        int64_t G = P.U / q;
+        if (G > p.grid) G = p.grid;
+        if (G > resident[dev]) G = resident[dev];
+        if (G < 1) G = 1;
+        P.G = (int)G;
+    }
+    a.coresident = P.G <= resident[dev] ? 1 : 0;
+    const int grid = P.G;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(kTcThreads, 1, 1);
@@ -553,27 +648,16 @@ int launch_tc(const nk_plan& p, const GemmArgs& in, cudaStream_t s) {
     P.KB = KB;
     P.U = (int64_t)p.n_tiles * m_tiles * KB;
     P.split = p.split_k;
-    if (p.split_k > 0) {
-        P.G = p.n_tiles * m_tiles * p.split_k;
-    } else {
-        // Keep at least the plan's units per CTA, so no tile is shared by more CTAs than the
-        // plan's `segments` (the workspace was sized for that).
-        const int64_t U_plan = (int64_t)p.n_tiles * p.m_tiles * KB;
-        const int64_t q = U_plan / p.grid;
-        int64_t G = P.U / q;
-        if (G > p.grid) G = p.grid;
-        if (G < 1) G = 1;
-        P.G = (int)G;
-    }
+    P.G = 1;  // set by launch_tc_t once the device's residency is known
     CUtensorMap mw, mx;
     if (make_map(&mw, a.w, a.N, a.K, a.ldw, kTcRows) != NK_OK) return NK_ERR_ALIGN;
     if (make_map(&mx, a.x, a.M, a.K, a.ldx, nt) != NK_OK) return NK_ERR_ALIGN;
     switch (nt) {
-        case 16: return launch_tc_t<16>(P.G, a, mw, mx, s);
-        case 32: return launch_tc_t<32>(P.G, a, mw, mx, s);
-        case 64: return launch_tc_t<64>(P.G, a, mw, mx, s);
-        case 128: return launch_tc_t<128>(P.G, a, mw, mx, s);
-        case 256: return launch_tc_t<256>(P.G, a, mw, mx, s);
+        case 16: return launch_tc_t<16>(p, a, mw, mx, s);
+        case 32: return launch_tc_t<32>(p, a, mw, mx, s);
+        case 64: return launch_tc_t<64>(p, a, mw, mx, s);
+        case 128: return launch_tc_t<128>(p, a, mw, mx, s);
+        case 256: return launch_tc_t<256>(p, a, mw, mx, s);
         default: return NK_ERR_PLAN;
     }
 }

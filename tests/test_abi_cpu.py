@@ -147,6 +147,27 @@ def check_tc_partition(p, M_max):
         for t in range(T):
             nseg = P.cta_of((t + 1) * P.KB - 1) - P.cta_of(t * P.KB) + 1
             assert 1 <= nseg <= p.segments, (t, nseg, p.segments)
+        # The finishing protocol of nk_tc.cu relies on: in every CTA's range, a partial
+        # segment of rank 0 (it holds the tile's first K block) can only be the CTA's last
+        # segment, and one of rank >= 1 only its first; so a waiting rank-0 CTA only waits for
+        # higher CTAs that publish before they could wait themselves.
+        for c in range(P.G):
+            b, e = P.begin(c), P.begin(c + 1)
+            u, segs = b, []
+            while u < e:
+                t = u // P.KB
+                end = min(e, (t + 1) * P.KB)
+                whole = (u == t * P.KB and end == (t + 1) * P.KB)
+                rank = c - P.cta_of(t * P.KB)
+                segs.append((whole, rank))
+                u = end
+            for i, (whole, rank) in enumerate(segs):
+                if whole:
+                    assert rank == 0
+                elif rank == 0:
+                    assert i == len(segs) - 1, (c, segs)
+                else:
+                    assert i == 0, (c, segs)
 
 
 @pytest.mark.parametrize("N,K", [(6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288),
