@@ -251,16 +251,11 @@ def main():
     ap.add_argument("--single", default=None,
                     help="N,K,M: run one decode linear --reps times and exit (profiler captures)")
     ap.add_argument("--reps", type=int, default=3)
-    ap.add_argument("--decode-step", type=int, default=0,
-                    help="B: run --reps fused Qwen3-8B decode steps at batch B, KV 1024, and exit "
-                         "(profiler captures of the whole step)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
     if args.single:
         return single(args)
-    if args.decode_step:
-        return decode_step_only(args)
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
 
@@ -497,15 +492,13 @@ def decode_bench(nk, dev, batches, world, local, kv=1024, steps=20, warmup=3):
     w = qwen3.Qwen3Weights(qwen3.QWEN3_8B, seed=7, device=dev)
     out = {"model": "qwen3-8b random-init, 36 layers, vocab 151936", "kv_length": kv,
            "steps": steps, "timing": "CUDA events around graph replays, max over ranks"}
-    arms = (("neokernel_b200", nk.mm, True, qwen3.PREFETCH_BYTES),
-            ("neokernel_b200_no_prefetch", nk.mm, True, None),
-            ("fused_ops_torch_mm", torch.mm, True, None),
-            ("torch_ops_torch_mm", torch.mm, False, None))
-    for name, linear, fused, prefetch in arms:
+    arms = (("neokernel_b200", nk.mm, True), ("fused_ops_torch_mm", torch.mm, True),
+            ("torch_ops_torch_mm", torch.mm, False))
+    for name, linear, fused in arms:
         res = {}
         for B in batches:
             g = qwen3.GraphDecoder(w, B, kv + warmup + steps + 1, linear, device=dev,
-                                   fused=fused, prefetch=prefetch)
+                                   fused=fused)
             gen = torch.Generator(device=dev).manual_seed(B)
             for c in g.st.k_cache + g.st.v_cache:
                 c.normal_(generator=gen)
@@ -572,22 +565,6 @@ def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, war
             "tp": world, "kv_length": kv, "steps": steps, "batches": res,
             "collectives": "fp32 all-reduce after o_proj and down, all-gather of (max, index) "
                            "for the vocab-split argmax; NCCL, captured in the CUDA graph"}
-
-
-def decode_step_only(args, kv=1024):
-    """--reps graph replays of the fused Qwen3-8B decode step at batch --decode-step, KV 1024."""
-    import neokernel_b200 as nk
-    from neokernel_b200 import qwen3
-    dev = torch.device("cuda", 0)
-    B = args.decode_step
-    w = qwen3.Qwen3Weights(qwen3.QWEN3_8B, seed=7, device=dev)
-    g = qwen3.GraphDecoder(w, B, kv + args.reps + 1, nk.mm, device=dev, fused=True)
-    g.st.position.fill_(kv)
-    for _ in range(args.reps):
-        g.step()
-    torch.cuda.synchronize(dev)
-    print(json.dumps({"decode_step": B, "reps": args.reps}))
-    return 0
 
 
 def _traffic_per_launch(avg_bytes):

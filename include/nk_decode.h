@@ -56,12 +56,6 @@ NK_API int nk_attention_decode_bf16(const void* q, const void* k_cache, const vo
 NK_API int nk_silu_mul_bf16(const void* gate_up, void* out, int rows, int intermediate,
                             nk_stream_t stream);
 
-/* Ask the memory system to stage [ptr, ptr + bytes) in L2 (16-byte aligned and sized): the
- * next decode linear's weights, issued while latency-bound kernels leave HBM idle. Returns
- * once the prefetches are issued; nothing waits for them and later kernels may start at
- * once. No counterpart in the reference (its linears always read weights from HBM). */
-NK_API int nk_prefetch_l2(const void* ptr, size_t bytes, nk_stream_t stream);
-
 #ifdef __cplusplus
 }
 #endif

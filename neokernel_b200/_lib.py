@@ -37,7 +37,7 @@ PLAN_MAGIC = 0x4E4B4731
 EXPORTS = ("nk_plan_make", "nk_ws_bytes", "nk_ws_init", "nk_gemm_bf16", "nk_device_error",
            "nk_status_string", "nk_version", "nk_gemm_bf16_static", "nk_gemm_bf16_f32out",
            "nk_rmsnorm_bf16", "nk_qk_norm_rope_cache_bf16", "nk_attention_ws_bytes",
-           "nk_attention_decode_bf16", "nk_silu_mul_bf16", "nk_prefetch_l2")
+           "nk_attention_decode_bf16", "nk_silu_mul_bf16")
 
 
 class NkPlan(ctypes.Structure):
@@ -113,8 +113,6 @@ def load() -> ctypes.CDLL:
     L.nk_attention_decode_bf16.restype = i32
     L.nk_silu_mul_bf16.argtypes = [vp, vp, i32, i32, vp]
     L.nk_silu_mul_bf16.restype = i32
-    L.nk_prefetch_l2.argtypes = [vp, ctypes.c_size_t, vp]
-    L.nk_prefetch_l2.restype = i32
     L.nk_device_error.argtypes = [vp, ctypes.POINTER(i32)]
     L.nk_device_error.restype = i32
     L.nk_status_string.argtypes = [i32]

@@ -303,30 +303,6 @@ silu_mul_kernel(const __nv_bfloat16* gate_up, __nv_bfloat16* out, int rows, int 
     *reinterpret_cast<uint4*>(out + row * I + i) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// ---------------------------------------------------------------------------------------
-// L2 prefetch of a read-only range (the next decode linear's weights) while latency-bound
-// kernels leave HBM idle. One thread per CTA issues cp.async.bulk.prefetch.L2 over its
-// share; nothing waits for the prefetches, so the grid finishes as soon as they are issued.
-// It is launched with ordinary stream ordering — it starts only once its predecessor has
-// completed — so that a successor's griddepcontrol.wait on this grid still implies every
-// earlier kernel has completed; it lets that successor launch at once.
-// ---------------------------------------------------------------------------------------
-constexpr int kPrefetchCtas = 148;
-constexpr uint32_t kPrefetchChunk = 64 * 1024;
-
-__global__ void __launch_bounds__(32) prefetch_l2_kernel(const char* base, size_t bytes) {
-    if (threadIdx.x != 0) return;
-    griddep_launch_dependents();
-    const size_t share = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~(size_t)15;
-    const size_t b0 = (size_t)blockIdx.x * share;
-    const size_t b1 = b0 + share < bytes ? b0 + share : bytes;
-    for (size_t off = b0; off < b1; off += kPrefetchChunk) {
-        const uint32_t n = (uint32_t)((b1 - off) < kPrefetchChunk ? (b1 - off) : kPrefetchChunk);
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"(n)
-                     : "memory");
-    }
-}
-
 static bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 }  // namespace nk
@@ -424,13 +400,4 @@ extern "C" int nk_silu_mul_bf16(const void* gate_up, void* out, int rows, int in
     return launch_pdl_smem(silu_mul_kernel, dim3(blocks), dim3(256), 0, (cudaStream_t)stream,
                            static_cast<const __nv_bfloat16*>(gate_up),
                            static_cast<__nv_bfloat16*>(out), rows, intermediate);
-}
-
-extern "C" int nk_prefetch_l2(const void* ptr, size_t bytes, nk_stream_t stream) {
-    if (bytes == 0) return NK_OK;
-    if (!ptr) return NK_ERR_ARG;
-    if (!al16(ptr) || (bytes & 15u)) return NK_ERR_ALIGN;
-    prefetch_l2_kernel<<<kPrefetchCtas, 32, 0, (cudaStream_t)stream>>>(
-        static_cast<const char*>(ptr), bytes);
-    return cudaGetLastError() == cudaSuccess ? NK_OK : NK_ERR_CUDA;
 }

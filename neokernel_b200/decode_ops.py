@@ -105,14 +105,3 @@ def silu_mul(gate_up: torch.Tensor, out: torch.Tensor):
                                        out.shape[1], _stream(out))
     if st != _lib.NK_OK:
         _raise(st, "nk_silu_mul_bf16")
-
-
-def prefetch_l2(t: torch.Tensor, nbytes: int | None = None):
-    """Stage the first ``nbytes`` (default all) of ``t``'s storage in L2 ahead of its use."""
-    n = t.numel() * t.element_size() if nbytes is None else min(nbytes, t.numel() * t.element_size())
-    n &= ~15
-    if n <= 0:
-        return
-    st = _lib.load().nk_prefetch_l2(t.data_ptr(), n, _stream(t))
-    if st != _lib.NK_OK:
-        _raise(st, "nk_prefetch_l2")

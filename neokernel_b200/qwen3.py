@@ -201,40 +201,24 @@ def layer_step(st: DecodeState, w: LayerWeights, k_cache, v_cache, d: Qwen3Dims,
     torch.add(st.x, st.branch, out=st.x)
 
 
-# L2 prefetch budget per latency-bound gap (bytes of the next linear's weights staged in the
-# 126 MB L2 while norm / RoPE / attention / SiLU kernels leave HBM idle); 0 disables.
-PREFETCH_BYTES = {"o": 64 << 20, "gate_up": 32 << 20, "down": 16 << 20, "qkv": 32 << 20}
-
-
 def layer_step_fused(st: DecodeState, w: LayerWeights, k_cache, v_cache, d: Qwen3Dims, linear,
-                     row_linear=None, carry=False, next_qkv=None, prefetch=None):
+                     row_linear=None, carry=False):
     """The same layer on the fused kernels (neokernel_b200.decode_ops), with the reference's
     fuse_norm_residual scheme (engine/kernels/decode.py:42-68): the down projection's output
-    stays in ``branch`` and the next RMSNorm adds it into ``x`` (``carry``). With ``prefetch``
-    (bytes per gap), each gap between linears first stages part of the next linear's weights
-    in L2 (``next_qkv``: the following layer's QKV weight)."""
+    stays in ``branch`` and the next RMSNorm adds it into ``x`` (``carry``)."""
     from . import decode_ops as ops
     row_linear = row_linear or linear
-    pf = prefetch or {}
     ops.rmsnorm(st.x, w.input_norm, st.norm, d.eps, branch=st.branch if carry else None)
     linear(st.norm, w.qkv, out=st.qkv)                                   # decode.py:54
-    if pf.get("o"):
-        ops.prefetch_l2(w.o_weight, pf["o"])
     ops.qk_norm_rope_cache(st.qkv, w.q_norm, w.k_norm, st.cos, st.sin, st.position, st.q,
                            k_cache, v_cache, d.heads, d.kv_heads, d.eps)
     ops.attention_decode(st.q, k_cache, v_cache, st.position, st.attn, st.attn_ws,
                          d.heads, d.kv_heads)
     row_linear(st.attn, w.o, out=st.branch)                              # decode.py:58
-    if pf.get("gate_up"):
-        ops.prefetch_l2(w.gate_up_weight, pf["gate_up"])
     ops.rmsnorm(st.x, w.post_norm, st.norm, d.eps, branch=st.branch)
     linear(st.norm, w.gate_up, out=st.gate_up)                           # decode.py:64
-    if pf.get("down"):
-        ops.prefetch_l2(w.down_weight, pf["down"])
     ops.silu_mul(st.gate_up, st.product)
     row_linear(st.product, w.down, out=st.branch)                        # decode.py:66
-    if pf.get("qkv") and next_qkv is not None:
-        ops.prefetch_l2(next_qkv, pf["qkv"])
 
 
 def greedy_head(st: DecodeState, lm_head, linear):
@@ -243,7 +227,7 @@ def greedy_head(st: DecodeState, lm_head, linear):
 
 
 def decode_step(st: DecodeState, w: Qwen3Weights, linear, row_linear=None, head=None,
-                fused=False, prefetch=None):
+                fused=False):
     """One greedy decode step for every sequence at ``st.position``; writes ``st.next_tokens``.
 
     ``row_linear`` (o_proj, down) and ``head`` (lm_head + argmax) are the hooks the
@@ -256,9 +240,8 @@ def decode_step(st: DecodeState, w: Qwen3Weights, linear, row_linear=None, head=
         if st.attn_ws is None:
             st.attn_ws = ops.attention_workspace(st.batch, d.heads, st.capacity, st.x.device)
         for i, lw in enumerate(w.layers):
-            nxt = w.layers[i + 1].qkv_weight if i + 1 < len(w.layers) else None
             layer_step_fused(st, lw, st.k_cache[i], st.v_cache[i], d, linear, row_linear,
-                             carry=i > 0, next_qkv=nxt, prefetch=prefetch)
+                             carry=i > 0)
         ops.rmsnorm(st.x, w.final_norm, st.norm, d.eps,
                     branch=st.branch if w.layers else None)
     else:
@@ -274,15 +257,14 @@ class GraphDecoder:
     engine/engine.py:119-129: side-stream warm-up x3, then capture) and replayed per token."""
 
     def __init__(self, w: Qwen3Weights, batch: int, capacity: int, linear, device="cuda",
-                 make_hooks=None, fused=False, prefetch=None):
+                 make_hooks=None, fused=False):
         """``make_hooks(state) -> (row_linear, head)`` supplies the tensor-parallel hooks,
         built once per state so their buffers are fixed before capture; ``fused`` selects the
         fused CUDA kernels for the non-linear ops."""
         self.w, self.linear = w, linear
         self.st = DecodeState(w, batch, capacity, device)
         row_linear, head = make_hooks(self.st) if make_hooks else (None, None)
-        step = lambda: decode_step(self.st, w, linear, row_linear, head, fused,  # noqa: E731
-                                   prefetch)
+        step = lambda: decode_step(self.st, w, linear, row_linear, head, fused)  # noqa: E731
         stream = torch.cuda.Stream(device=device)
         self.stream = stream
         stream.wait_stream(torch.cuda.current_stream(device))
