@@ -251,11 +251,16 @@ def main():
     ap.add_argument("--single", default=None,
                     help="N,K,M: run one decode linear --reps times and exit (profiler captures)")
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--decode-step", type=int, default=0,
+                    help="B: run --reps fused Qwen3-8B decode steps at batch B, KV 1024, and exit "
+                         "(profiler captures of the whole step)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
     if args.single:
         return single(args)
+    if args.decode_step:
+        return decode_step_only(args)
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
 
@@ -565,6 +570,22 @@ def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, war
             "tp": world, "kv_length": kv, "steps": steps, "batches": res,
             "collectives": "fp32 all-reduce after o_proj and down, all-gather of (max, index) "
                            "for the vocab-split argmax; NCCL, captured in the CUDA graph"}
+
+
+def decode_step_only(args, kv=1024):
+    """--reps graph replays of the fused Qwen3-8B decode step at batch --decode-step, KV 1024."""
+    import neokernel_b200 as nk
+    from neokernel_b200 import qwen3
+    dev = torch.device("cuda", 0)
+    B = args.decode_step
+    w = qwen3.Qwen3Weights(qwen3.QWEN3_8B, seed=7, device=dev)
+    g = qwen3.GraphDecoder(w, B, kv + args.reps + 1, nk.mm, device=dev, fused=True)
+    g.st.position.fill_(kv)
+    for _ in range(args.reps):
+        g.step()
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"decode_step": B, "reps": args.reps}))
+    return 0
 
 
 def _traffic_per_launch(avg_bytes):

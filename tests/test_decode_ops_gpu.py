@@ -157,3 +157,4 @@ def test_fused_step_matches_unfused_step():
         # with the deferred residual the fused state holds x before the last down output;
         # the final norm added it, so the final normalised rows agree
         assert (a.norm.float() - b.norm.float()).abs().max().item() <= 0.05
+
