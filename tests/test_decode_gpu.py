@@ -113,10 +113,12 @@ def test_qwen3_8b_128_greedy_tokens(batch):
     assert torch.isfinite(ref_logits).all()
     assert float(m.max()) <= MARGIN, report
     # Up to its first divergence a sequence has seen identical inputs on both paths, so the
-    # token that differs there must be a near-tie of the reference's own logits: within a
-    # few bf16 ulps (ulp = 1/32 for logits in [4, 8)).
+    # token that differs there must be a near-tie of the reference's own logits: within the
+    # logit noise another valid fp32-accumulating GEMM shows on the same inputs (the control's
+    # teacher-forced max logit difference), and never beyond 8 bf16 ulps at |logit| < 8.
+    tie_bound = min(max(0.125, float((lc - lr).abs().max())), 0.25)
     for b in range(batch):
         if first_diff[b] is not None:
-            assert float(m[b, first_diff[b]]) <= 0.125, report
+            assert float(m[b, first_diff[b]]) <= tie_bound, report
     del ours, ref, ctrl
     torch.cuda.empty_cache()
