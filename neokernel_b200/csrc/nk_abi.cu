@@ -110,7 +110,12 @@ extern "C" int nk_plan_make(nk_plan* p, int M_max, int N, int K, int split_k, in
             p->segments = split;
             p->k_slice = ceil_div(KB, split) * kTcKStep;
         } else {
-            const int64_t slots = (int64_t)kNumSMs * tc_ctas_per_sm(p->tile_m);
+            // A second CTA per SM pays only while each CTA keeps enough units: below that the
+            // extra split tiles cost more finishing work, and a full SM leaves no room for
+            // the next launch's prologue and first weight loads to overlap this one's tail.
+            int per_sm = tc_ctas_per_sm(p->tile_m);
+            if (per_sm > 1 && U < (int64_t)kNumSMs * per_sm * NK_TC_DUAL_MIN_UNITS) per_sm = 1;
+            const int64_t slots = (int64_t)kNumSMs * per_sm;
             const int64_t G = U < slots ? U : slots;
             const int64_t q = U / G;  // units per CTA (the last ones may have one more)
             const int64_t seg = 1 + (KB - 1 + q - 1) / q;

@@ -240,6 +240,10 @@ constexpr int kTcBox = 64;               // K elements per TMA box (one 128-byte
 #endif
 constexpr int kTcBoxesPerStage = NK_TC_UK;           // TMA boxes along K per pipeline stage
 constexpr int kTcKStep = kTcBox * kTcBoxesPerStage;  // K elements per stage (one unit)
+// fewest units per CTA for which the plan puts two CTAs on an SM (when both fit)
+#ifndef NK_TC_DUAL_MIN_UNITS
+#define NK_TC_DUAL_MIN_UNITS 16
+#endif
 constexpr int kGenericRows = 8;          // rows per CTA in the generic kernel
 constexpr int kGenericTokens = 8;        // tokens per CTA in the generic kernel
 

@@ -224,10 +224,12 @@ __device__ __forceinline__ Segment segment_at(int64_t u, int64_t u_end, int KB) 
 }
 
 // Every CTA of the grid must be resident at once (rank-0 CTAs of shared tiles wait for
-// higher CTAs), so the register budget must allow TcSmem<NT>::kPerSm CTAs per SM, and the
-// launch caps the grid by the occupancy the runtime reports.
+// higher CTAs), and the launch caps the grid by the CTAs that fit per SM. Two CTAs of six
+// warps per SM need at most 128 registers a thread (each SM sub-partition holds up to four
+// of the twelve warps), hence the cap for the token tiles that fit twice in shared memory.
+#define NK_TC_MAXNREG 128
 template <int NT>
-__global__ void __launch_bounds__(kTcThreads, TcSmem<NT>::kPerSm)
+__global__ void __launch_bounds__(kTcThreads) __maxnreg__(NT <= 64 ? NK_TC_MAXNREG : 255)
 tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
           GemmArgs a) {
     using L = TcSmem<NT>;
@@ -438,7 +440,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                         if (c0 >= mcount) break;  // warp-uniform
                         float v[16];
                         tmem_ld16(taddr + c0, v);
-#pragma unroll 4
+#pragma unroll 2
                         for (int r = 1; r < nseg; ++r) {
                             const float* pr = slot0 + ((size_t)r * a.part_cols + c0) * kTcRows;
                             float p[16];
@@ -482,7 +484,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                             float v[16];
 #pragma unroll
                             for (int j = 0; j < 16; ++j) v[j] = 0.f;
-#pragma unroll 4
+#pragma unroll 2
                             for (int r = 0; r < nseg; ++r) {
                                 const float* pr = slot0 + ((size_t)r * a.part_cols + c0) * kTcRows;
                                 float p[16];
@@ -582,11 +584,45 @@ int tc_ctas_per_sm(int nt) {
     }
 }
 
+// CTAs of tc_kernel<NT> that fit on one SM at once. The runtime's occupancy query answers 1
+// for every kernel that executes tcgen05.alloc (on B200 even for a 12-register kernel), but
+// the block scheduler places such CTAs by registers, shared memory and threads: 296 CTAs
+// that each hold 32 TMEM columns run on 148 SMs as one wave, two overlapping on every SM.
+// So the count is made here from those limits, plus the 512 TMEM columns of an SM (so no
+// CTA blocks in tcgen05.alloc), and capped at the per-SM count the stage budget assumes.
+template <int NT>
+static int tc_resident_per_sm(int dev) {
+    using L = TcSmem<NT>;
+    cudaFuncAttributes fa;
+    int smem_sm = 0, reserved = 0, regs_sm = 0, thr_sm = 0;
+    if (cudaFuncGetAttributes(&fa, tc_kernel<NT>) != cudaSuccess ||
+        cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) !=
+            cudaSuccess ||
+        cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) !=
+            cudaSuccess ||
+        cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev) !=
+            cudaSuccess ||
+        cudaDeviceGetAttribute(&thr_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev) !=
+            cudaSuccess)
+        return 0;
+    constexpr int kWarps = kTcThreads / 32;
+    // registers: 8-register steps per thread, and each of the 4 sub-partitions holds its
+    // quarter of the register file for at most ceil(warps / 4) warps of every CTA
+    const int regs_warp = ((fa.numRegs + 7) & ~7) * 32;
+    const int by_regs = (regs_sm / 4) / (regs_warp * ((kWarps + 3) / 4));
+    const int by_smem = smem_sm / (L::kAlloc + (int)fa.sharedSizeBytes + reserved);
+    const int by_thr = thr_sm / kTcThreads;
+    const int by_tmem = 512 / L::kTmemCols;
+    int n = L::kPerSm;
+    for (int lim : {by_regs, by_smem, by_thr, by_tmem}) n = lim < n ? lim : n;
+    return n;
+}
+
 template <int NT>
 static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
                        const CUtensorMap& mx, cudaStream_t s) {
     using L = TcSmem<NT>;
-    static int resident[64] = {};  // co-resident CTAs per device (0 = not yet queried)
+    static int resident[64] = {};  // co-resident CTAs per device (0 = not yet counted)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return NK_ERR_CUDA;
     if (dev < 0 || dev >= 64) return NK_ERR_DEVICE;
@@ -596,11 +632,10 @@ static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
             cudaFuncSetAttribute(tc_kernel<NT>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return NK_ERR_CUDA;
-        int per_sm = 0, sms = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tc_kernel<NT>, kTcThreads,
-                                                          L::kAlloc) != cudaSuccess ||
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
             return NK_ERR_CUDA;
+        const int per_sm = tc_resident_per_sm<NT>(dev);
         if (per_sm < 1) return NK_ERR_CUDA;
         resident[dev] = per_sm * sms;
     }
