@@ -160,30 +160,120 @@ qk_norm_rope_cache_kernel(const __nv_bfloat16* qkv, int64_t ld_qkv, const __nv_b
 // ---------------------------------------------------------------------------------------
 // Grouped split-KV decode attention. CTA (split, kv head, sequence) covers cache positions
 // [split*C, split*C + C) clipped to [0, position] for all G = Hq/Hkv query heads that share
-// the KV head, so each K/V row is read once per group. Four warps take every fourth position
-// with an online softmax per query head (lane l holds elements 4l..4l+3); the warps' states
-// are combined in shared memory and the CTA stores (max, sum, unnormalised acc). A merge
-// kernel combines the splits: out = sum_s e^(m_s-M) acc_s / sum_s e^(m_s-M) l_s.
+// the KV head, so each K/V row is read once per group.
+//
+// Decode attention moves a few MB per layer, so its time is DRAM latency unless many loads
+// are in flight: every thread first issues its share of the chunk's K rows, then of its V
+// rows, as asynchronous copies into shared memory (16 or 8 bytes each; rows past the
+// position are zero-filled without a read), so the whole 2 x 16 KB chunk is requested at
+// once. Warp w then scores rows [16w, 16w + 16) in two batches of 8: lane l forms the
+// partial dot products of elements 4l..4l+3, a recursive-halving reduction leaves each
+// (row, head) score on its owner lanes, which alone evaluate the exponentials of the
+// online softmax and pass the batch's probabilities to the whole warp through shared
+// memory for the V accumulation (lane l again holding elements 4l..4l+3). The warps' states are combined in shared memory
+// and the CTA stores (max, sum, unnormalised acc); a merge kernel combines the splits:
+// out = sum_s e^(m_s-M) acc_s / sum_s e^(m_s-M) l_s. CTAs whose chunk starts past the
+// position store nothing (the merge reads only the splits at or below it).
 // ---------------------------------------------------------------------------------------
 constexpr int kAttnChunk = 64;
 constexpr int kAttnThreads = 128;
 constexpr int kAttnMaxGroup = 8;
+constexpr int kAttnBatch = 8;                       // rows scored together by a warp
+constexpr int kAttnRowBytes = kHeadDim * 2;         // 256 B per cache row
+constexpr int kAttnTileBytes = kAttnChunk * kAttnRowBytes;  // 16 KB per K or V chunk
+
+template <int VB>
+__device__ __forceinline__ void cp_async(uint32_t dst, const void* src, bool valid) {
+    const int n = valid ? VB : 0;  // 0 source bytes: the destination is zero-filled
+    if constexpr (VB == 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n)
+                     : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(n)
+                     : "memory");
+}
+
+// Copies rows [0, C) of one cache chunk into a [C][128] bf16 tile; rows >= valid are zeros.
+template <int VB>
+__device__ __forceinline__ void attn_load_tile(uint32_t tile, const __nv_bfloat16* rows0,
+                                               int64_t cs, int valid) {
+    constexpr int kSegs = kAttnRowBytes / VB;  // copies per row
+#pragma unroll
+    for (int i = 0; i < kAttnChunk * kSegs / kAttnThreads; ++i) {
+        const int idx = i * kAttnThreads + threadIdx.x;
+        const int row = idx / kSegs, seg = idx - row * kSegs;
+        const bool ok = row < valid;
+        const __nv_bfloat16* src = rows0 + (int64_t)(ok ? row : 0) * cs + seg * (VB / 2);
+        cp_async<VB>(tile + row * kAttnRowBytes + seg * VB, src, ok);
+    }
+}
+
+// Sums the 8 x G scores of a batch (value i = r * G + g, one partial per lane) across the
+// warp by recursive halving: at offset o a lane keeps the half of its values selected by
+// bit o of its lane id and adds the partner's copy of that half, so 8G values need 8G - 1
+// shuffles instead of 5 * 8G. Afterwards lane l holds the full sums of rows r = l >> 2 and
+// heads g = own_head(l, j), j < kOwned (duplicated over the low lane bits when G < 4).
+template <int G>
+struct AttnOwn {
+    static constexpr int kValues = kAttnBatch * G;
+    static constexpr int kOwned = G == 8 ? 2 : 1;
+    static constexpr int kLog2G = G == 8 ? 3 : G == 4 ? 2 : G == 2 ? 1 : 0;
+    __device__ static __forceinline__ int head(int lane, int j) {
+        return G == 8 ? 2 * (lane & 3) + j : (lane >> (2 - kLog2G)) & (G - 1);
+    }
+};
 
 template <int G>
+__device__ __forceinline__ void attn_reduce_scores(float (&v)[kAttnBatch * G], int lane) {
+    constexpr int NV = kAttnBatch * G;
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+        const int o = 16 >> k;
+        const int n = NV >> k;  // values still held before this step (constant once unrolled)
+        if (n > AttnOwn<G>::kOwned) {
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int j = 0; j < n / 2; ++j) {
+                const float send = up ? v[j] : v[j + n / 2];
+                const float keep = up ? v[j + n / 2] : v[j];
+                v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < AttnOwn<G>::kOwned; ++j) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
+        }
+    }
+}
+
+template <int G, int VB>
 __global__ void __launch_bounds__(kAttnThreads)
 attn_partial_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
                     const __nv_bfloat16* v_cache, const int64_t* position, float* part_acc,
-                    float* part_ml, int Hq, int Hkv, int splits, int64_t cb, int64_t ch,
-                    int64_t cs, float scale) {
+                    float* part_ml, int Hq, int Hkv, int splits, int capacity, int64_t cb,
+                    int64_t ch, int64_t cs, float scale) {
+    using O = AttnOwn<G>;
+    constexpr int NO = O::kOwned;
+    // K tile, V tile; after scoring, the K tile holds the warps' accumulators
+    __shared__ __align__(128) uint8_t s_tiles[2 * kAttnTileBytes];
+    __shared__ __align__(16) float s_p[4][kAttnBatch][G];  // a warp's batch probabilities
+    __shared__ __align__(16) float s_c[4][G];              // ... and running-sum rescales
     __shared__ float s_m[4][G], s_l[4][G];
-    __shared__ float s_acc[4][G][kHeadDim];
+    static_assert(4 * G * kHeadDim * 4 <= kAttnTileBytes, "accumulators must fit the K tile");
     if (threadIdx.x == 0) griddep_launch_dependents();
     griddep_wait();
     const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t pos = *position;
+    const int64_t pos = min(*position, (int64_t)capacity - 1);  // never past the cache
     const int j0 = split * kAttnChunk;
-    const int j1 = (int)min((int64_t)j0 + kAttnChunk, pos + 1);
+    if ((int64_t)j0 > pos) return;
+    const int valid = (int)min((int64_t)kAttnChunk, pos + 1 - j0);
+
+    const uint32_t sk = smem_u32(s_tiles), sv = sk + kAttnTileBytes;
+    const int64_t base = (int64_t)b * cb + (int64_t)kh * ch + (int64_t)j0 * cs;
+    attn_load_tile<VB>(sk, k_cache + base, cs, valid);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    attn_load_tile<VB>(sv, v_cache + base, cs, valid);
+    asm volatile("cp.async.commit_group;" ::: "memory");
 
     float qf[G][4];
 #pragma unroll
@@ -193,40 +283,93 @@ attn_partial_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
         qf[g][0] = bf16lo(qv.x); qf[g][1] = bf16hi(qv.x);
         qf[g][2] = bf16lo(qv.y); qf[g][3] = bf16hi(qv.y);
     }
-    float m[G], l[G], acc[G][4];
+    float acc[G][4];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        m[g] = -INFINITY; l[g] = 0.f;
-        acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
-    }
-    const __nv_bfloat16* kb = k_cache + (int64_t)b * cb + (int64_t)kh * ch + lane * 4;
-    const __nv_bfloat16* vb = v_cache + (int64_t)b * cb + (int64_t)kh * ch + lane * 4;
-    for (int j = j0 + warp; j < j1; j += 4) {
-        const uint2 kv = *reinterpret_cast<const uint2*>(kb + (int64_t)j * cs);
-        const uint2 vv = *reinterpret_cast<const uint2*>(vb + (int64_t)j * cs);
-        const float k0 = bf16lo(kv.x), k1 = bf16hi(kv.x), k2 = bf16lo(kv.y), k3 = bf16hi(kv.y);
-        const float v0 = bf16lo(vv.x), v1 = bf16hi(vv.x), v2 = bf16lo(vv.y), v3 = bf16hi(vv.y);
+    for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
+    float m_own[NO], l_own[NO];  // running max and sum of the heads this lane owns
+#pragma unroll
+    for (int j = 0; j < NO; ++j) { m_own[j] = -INFINITY; l_own[j] = 0.f; }
+    const int r_own = lane >> 2;
+    const uint8_t* kt = s_tiles + lane * 8;
+    const uint8_t* vt = s_tiles + kAttnTileBytes + lane * 8;
+
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // this thread's K copies landed
+    __syncthreads();                                     // ... and everyone's
+#pragma unroll
+    for (int bt = 0; bt < 2; ++bt) {
+        const int r0 = warp * 16 + bt * kAttnBatch;
+        float sc[O::kValues];
+#pragma unroll
+        for (int r = 0; r < kAttnBatch; ++r) {
+            const uint2 kv = *reinterpret_cast<const uint2*>(kt + (r0 + r) * kAttnRowBytes);
+            const float k0 = bf16lo(kv.x), k1 = bf16hi(kv.x), k2 = bf16lo(kv.y), k3 = bf16hi(kv.y);
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+                sc[r * G + g] = qf[g][0] * k0 + qf[g][1] * k1 + qf[g][2] * k2 + qf[g][3] * k3;
+        }
+        attn_reduce_scores<G>(sc, lane);
+        const bool row_ok = r0 + r_own < valid;
+#pragma unroll
+        for (int j = 0; j < NO; ++j) {
+            const float x = row_ok ? sc[j] * scale : -INFINITY;
+            float bm = x;  // batch max over the 8 rows (lane bits 2-4) of this head
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
+            const float mn = fmaxf(m_own[j], bm);
+            const bool any = mn != -INFINITY;
+            const float corr = any ? expf(m_own[j] - mn) : 1.f;  // 0 while m is still -inf
+            const float p = any ? expf(x - mn) : 0.f;            // 0 for rows past the position
+            float ps = p;
+            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+            l_own[j] = l_own[j] * corr + ps;
+            m_own[j] = mn;
+            const int g = O::head(lane, j);
+            s_p[warp][r_own][g] = p;
+            if (r_own == 0) s_c[warp][g] = corr;
+        }
+        if (bt == 0) {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");  // V copies landed
+            __syncthreads();
+        } else {
+            __syncwarp();
+        }
+        float vr[kAttnBatch][4];
+#pragma unroll
+        for (int r = 0; r < kAttnBatch; ++r) {
+            const uint2 vv = *reinterpret_cast<const uint2*>(vt + (r0 + r) * kAttnRowBytes);
+            vr[r][0] = bf16lo(vv.x); vr[r][1] = bf16hi(vv.x);
+            vr[r][2] = bf16lo(vv.y); vr[r][3] = bf16hi(vv.y);
+        }
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            float sc = qf[g][0] * k0 + qf[g][1] * k1 + qf[g][2] * k2 + qf[g][3] * k3;
-            sc = warp_sum(sc) * scale;
-            const float mn = fmaxf(m[g], sc);
-            const float corr = expf(m[g] - mn);  // 0 while m is still -inf
-            const float p = expf(sc - mn);
-            l[g] = l[g] * corr + p;
-            acc[g][0] = acc[g][0] * corr + p * v0;
-            acc[g][1] = acc[g][1] * corr + p * v1;
-            acc[g][2] = acc[g][2] * corr + p * v2;
-            acc[g][3] = acc[g][3] * corr + p * v3;
-            m[g] = mn;
+            const float c = s_c[warp][g];
+            float a0 = acc[g][0] * c, a1 = acc[g][1] * c, a2 = acc[g][2] * c, a3 = acc[g][3] * c;
+#pragma unroll
+            for (int r = 0; r < kAttnBatch; ++r) {
+                const float p = s_p[warp][r][g];
+                a0 += p * vr[r][0]; a1 += p * vr[r][1]; a2 += p * vr[r][2]; a3 += p * vr[r][3];
+            }
+            acc[g][0] = a0; acc[g][1] = a1; acc[g][2] = a2; acc[g][3] = a3;
+        }
+        __syncwarp();  // the next batch overwrites s_p and s_c
+    }
+    if (r_own == 0) {
+#pragma unroll
+        for (int j = 0; j < NO; ++j) {
+            const int g = O::head(lane, j);
+            s_m[warp][g] = m_own[j];
+            s_l[warp][g] = l_own[j];
         }
     }
+    __syncthreads();  // every warp is done with the K tile
+    float* s_acc = reinterpret_cast<float*>(s_tiles);  // [4][G][128]
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        if (lane == 0) { s_m[warp][g] = m[g]; s_l[warp][g] = l[g]; }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) s_acc[warp][g][lane * 4 + e] = acc[g][e];
-    }
+    for (int g = 0; g < G; ++g)
+        *reinterpret_cast<float4*>(s_acc + (warp * G + g) * kHeadDim + lane * 4) =
+            make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
     __syncthreads();
     // thread t combines element d = t of every query head of the group
     const int d = threadIdx.x;
@@ -236,13 +379,12 @@ attn_partial_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
 #pragma unroll
         for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w][g]);
         float L = 0.f, A = 0.f;
-        if (M != -INFINITY) {
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
-                const float f = expf(s_m[w][g] - M);
-                L += s_l[w][g] * f;
-                A += s_acc[w][g][d] * f;
-            }
+        for (int w = 0; w < 4; ++w) {
+            if (s_m[w][g] == -INFINITY) continue;  // a warp whose rows are all past the position
+            const float f = expf(s_m[w][g] - M);
+            L += s_l[w][g] * f;
+            A += s_acc[(w * G + g) * kHeadDim + d] * f;
         }
         const int64_t hrow = ((int64_t)b * Hq + kh * G + g) * splits + split;
         part_acc[hrow * kHeadDim + d] = A;
@@ -253,23 +395,38 @@ attn_partial_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
     }
 }
 
+// One CTA per (sequence, query head); thread d owns output element d. The splits' maxima are
+// gathered in parallel (one load per thread per 128 splits) and reduced across the CTA, then
+// the weighted sums run over the splits with their loads unrolled.
 __global__ void __launch_bounds__(kHeadDim)
 attn_merge_kernel(const float* part_acc, const float* part_ml, __nv_bfloat16* out, int splits,
-                  const int64_t* position) {
+                  int capacity, const int64_t* position) {
+    __shared__ float s_max[kHeadDim / 32];
     if (threadIdx.x == 0) griddep_launch_dependents();
     griddep_wait();
     const int64_t hrow = blockIdx.x;  // b * Hq + h
     const int d = threadIdx.x;
-    const int used = (int)min((int64_t)splits, *position / kAttnChunk + 1);
+    const int64_t pos = min(*position, (int64_t)capacity - 1);
+    const int used = (int)min((int64_t)splits, pos / kAttnChunk + 1);
+    const float* ml = part_ml + hrow * splits * 2;
+    const float* pa = part_acc + hrow * splits * kHeadDim + d;
     float M = -INFINITY;
-    for (int s = 0; s < used; ++s) M = fmaxf(M, part_ml[(hrow * splits + s) * 2]);
+    for (int s = d; s < used; s += kHeadDim) M = fmaxf(M, ml[s * 2]);
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 16));
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 8));
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 4));
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 2));
+    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 1));
+    if ((d & 31) == 0) s_max[d >> 5] = M;
+    __syncthreads();
+    M = fmaxf(fmaxf(s_max[0], s_max[1]), fmaxf(s_max[2], s_max[3]));
     float L = 0.f, A = 0.f;
+#pragma unroll 8
     for (int s = 0; s < used; ++s) {
-        const float ms = part_ml[(hrow * splits + s) * 2];
-        if (ms == -INFINITY) continue;
-        const float f = expf(ms - M);
-        L += part_ml[(hrow * splits + s) * 2 + 1] * f;
-        A += part_acc[(hrow * splits + s) * kHeadDim + d] * f;
+        const float ms = ml[s * 2];
+        const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+        L += ml[s * 2 + 1] * f;
+        A += pa[(int64_t)s * kHeadDim] * f;
     }
     out[hrow * kHeadDim + d] = __float2bfloat16_rn(A / L);
 }
@@ -377,17 +534,26 @@ extern "C" int nk_attention_decode_bf16(const void* q, const void* k_cache, cons
     const auto* qq = static_cast<const __nv_bfloat16*>(q);
     const auto* kk = static_cast<const __nv_bfloat16*>(k_cache);
     const auto* vv = static_cast<const __nv_bfloat16*>(v_cache);
+    // 16-byte copies when every cache row segment is 16-byte aligned, else 8-byte copies
+    const bool wide = al16(k_cache) && al16(v_cache) && cache_seq_stride % 8 == 0 &&
+                      cache_head_stride % 8 == 0 && cache_batch_stride % 8 == 0;
     int st;
+#define NK_ATTN_LAUNCH(GG, VB)                                                                  \
+    launch_pdl_smem(attn_partial_kernel<GG, VB>, grid, dim3(kAttnThreads), 0, s, qq, kk, vv,   \
+                    position, part_acc, part_ml, q_heads, kv_heads, splits, capacity,           \
+                    cache_batch_stride,                                                       \
+                    cache_head_stride, cache_seq_stride, scale)
     switch (G) {
-        case 1: st = launch_pdl_smem(attn_partial_kernel<1>, grid, dim3(kAttnThreads), 0, s, qq, kk, vv, position, part_acc, part_ml, q_heads, kv_heads, splits, cache_batch_stride, cache_head_stride, cache_seq_stride, scale); break;
-        case 2: st = launch_pdl_smem(attn_partial_kernel<2>, grid, dim3(kAttnThreads), 0, s, qq, kk, vv, position, part_acc, part_ml, q_heads, kv_heads, splits, cache_batch_stride, cache_head_stride, cache_seq_stride, scale); break;
-        case 4: st = launch_pdl_smem(attn_partial_kernel<4>, grid, dim3(kAttnThreads), 0, s, qq, kk, vv, position, part_acc, part_ml, q_heads, kv_heads, splits, cache_batch_stride, cache_head_stride, cache_seq_stride, scale); break;
-        default: st = launch_pdl_smem(attn_partial_kernel<8>, grid, dim3(kAttnThreads), 0, s, qq, kk, vv, position, part_acc, part_ml, q_heads, kv_heads, splits, cache_batch_stride, cache_head_stride, cache_seq_stride, scale); break;
+        case 1: st = wide ? NK_ATTN_LAUNCH(1, 16) : NK_ATTN_LAUNCH(1, 8); break;
+        case 2: st = wide ? NK_ATTN_LAUNCH(2, 16) : NK_ATTN_LAUNCH(2, 8); break;
+        case 4: st = wide ? NK_ATTN_LAUNCH(4, 16) : NK_ATTN_LAUNCH(4, 8); break;
+        default: st = wide ? NK_ATTN_LAUNCH(8, 16) : NK_ATTN_LAUNCH(8, 8); break;
     }
+#undef NK_ATTN_LAUNCH
     if (st != NK_OK) return st;
     return launch_pdl_smem(attn_merge_kernel, dim3(batch * q_heads), dim3(kHeadDim), 0, s,
                            (const float*)part_acc, (const float*)part_ml,
-                           static_cast<__nv_bfloat16*>(out), splits, position);
+                           static_cast<__nv_bfloat16*>(out), splits, capacity, position);
 }
 
 extern "C" int nk_silu_mul_bf16(const void* gate_up, void* out, int rows, int intermediate,

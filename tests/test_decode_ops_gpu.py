@@ -123,6 +123,45 @@ def test_attention_decode(B, H, Hkv, cap):
             assert torch.equal(out2, out)
 
 
+@pytest.mark.parametrize("H,Hkv", [(32, 8), (8, 1)])
+def test_attention_decode_8_byte_aligned_cache(H, Hkv):
+    """Caches whose rows are only 8-byte aligned (row pitch 132 elements, base offset 4)
+    take the 8-byte copy path and give the same result as a packed copy."""
+    B, cap = 2, 150
+    d = qwen3.Qwen3Dims(1024, 1024, H, Hkv, 128, 1, 64)
+    kst = rand(B, Hkv, cap, 132, seed=11)
+    vst = rand(B, Hkv, cap, 132, seed=12)
+    kc, vc = kst[..., 4:], vst[..., 4:]
+    assert kc.data_ptr() % 16 == 8 and kc.stride(2) == 132
+    kp, vp = kc.contiguous(), vc.contiguous()
+    ws = ops.attention_workspace(B, H, cap, DEV)
+    slots = torch.arange(cap, device=DEV)
+    for pos in (0, 70, cap - 1):
+        q = rand(B, H * 128, seed=200 + pos)
+        position = torch.tensor([pos], device=DEV)
+        out, out_p = torch.empty_like(q), torch.empty_like(q)
+        ops.attention_decode(q, kc, vc, position, out, ws, H, Hkv)
+        ops.attention_decode(q, kp, vp, position, out_p, ws, H, Hkv)
+        torch.cuda.synchronize()
+        assert torch.equal(out, out_p)
+        ref = qwen3.attention(q.view(B, H, 128), kp, vp, position, slots, d)
+        close(out, ref, abs_slack=4e-3, exact_frac=0.97)
+
+
+def test_attention_decode_position_clamped_to_capacity():
+    """A position past the cache attends over the whole cache, reading nothing beyond it."""
+    B, H, Hkv, cap = 2, 32, 8, 100
+    kc = rand(B, Hkv, cap, 128, seed=13)
+    vc = rand(B, Hkv, cap, 128, seed=14)
+    ws = ops.attention_workspace(B, H, cap, DEV)
+    q = rand(B, H * 128, seed=15)
+    a, b = torch.empty_like(q), torch.empty_like(q)
+    ops.attention_decode(q, kc, vc, torch.tensor([cap - 1], device=DEV), a, ws, H, Hkv)
+    ops.attention_decode(q, kc, vc, torch.tensor([cap + 37], device=DEV), b, ws, H, Hkv)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
 @pytest.mark.parametrize("rows", (1, 16))
 @pytest.mark.parametrize("I", (8, 3072, 12288))
 def test_silu_mul(rows, I):
