@@ -25,13 +25,15 @@ NK_API int nk_rmsnorm_bf16(void* x, const void* branch, const void* weight, void
 /* Per-head RMSNorm of the query and key heads of the packed qkv row, RoPE with the bf16
  * cos/sin tables [capacity, head_dim] at *position (each product rounded, then the sum),
  * query heads to q_out [batch, q_heads * head_dim], key and value heads into the caches at
- * slot *position (strides in elements). head_dim must be 128. Replaces
+ * slot *position (strides in elements); cos_table and sin_table hold [capacity, 128]. head_dim
+ * must be 128. A *position outside [0, capacity) writes nothing and sets the device error
+ * word to NK_ERR_RANGE (nk_device_error). Replaces
  * qk_rope_cache_out(..., fused=True) at engine/kernels/elementwise.py:63-78. */
 NK_API int nk_qk_norm_rope_cache_bf16(const void* qkv, int64_t ld_qkv, const void* q_norm,
                                       const void* k_norm, const void* cos_table,
                                       const void* sin_table, const int64_t* position,
                                       void* q_out, void* k_cache, void* v_cache, int batch,
-                                      int q_heads, int kv_heads, int head_dim,
+                                      int q_heads, int kv_heads, int head_dim, int capacity,
                                       int64_t cache_batch_stride, int64_t cache_head_stride,
                                       int64_t cache_seq_stride, float eps, nk_stream_t stream);
 
@@ -41,7 +43,9 @@ NK_API size_t nk_attention_ws_bytes(int batch, int q_heads, int capacity);
 /* Grouped split-KV decode attention over cache slots [0, *position]: out[b, h] =
  * softmax(q[b,h] . K[b, h/G]^T * scale) V[b, h/G] with fp32 scores, softmax and sums,
  * rounded once to bf16. q, out: [batch, q_heads, 128]; caches [batch, kv_heads, capacity,
- * 128] with the given strides; G = q_heads / kv_heads in {1, 2, 4, 8}. Replaces
+ * 128] with the given strides (q and caches 8-byte aligned, strides multiples of 4); G =
+ * q_heads / kv_heads in {1, 2, 4, 8}. A *position >= capacity attends over the whole cache and
+ * a negative one writes nothing; both set the device error word to NK_ERR_RANGE. Replaces
  * attention_out(q, k, v, position, out, partial, lse) at engine/kernels/attention.py:53-62. */
 NK_API int nk_attention_decode_bf16(const void* q, const void* k_cache, const void* v_cache,
                                     const int64_t* position, void* out, int batch, int q_heads,

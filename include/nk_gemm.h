@@ -58,6 +58,8 @@ typedef struct CUstream_st* nk_stream_t; /* identical to cudaStream_t */
 #define NK_ERR_DEVICE     -7  /* current device is not sm_100 (B200 class)                */
 #define NK_ERR_TIMEOUT    -8  /* a kernel's bounded wait expired (read by nk_device_error) */
 #define NK_ERR_ARG        -9  /* any other invalid argument                               */
+#define NK_ERR_RANGE      -10 /* a device-side decode position outside its cache (read by
+                                  nk_device_error)                                       */
 
 /* Kernel families a plan can select. */
 #define NK_KIND_AUTO     0

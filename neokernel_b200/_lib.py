@@ -25,6 +25,7 @@ NK_ERR_CUDA = -6
 NK_ERR_DEVICE = -7
 NK_ERR_TIMEOUT = -8
 NK_ERR_ARG = -9
+NK_ERR_RANGE = -10
 
 KIND_AUTO = 0
 KIND_GEMV = 1
@@ -104,7 +105,7 @@ def load() -> ctypes.CDLL:
     L.nk_rmsnorm_bf16.argtypes = [vp, vp, vp, vp, i32, i32, f32, vp]
     L.nk_rmsnorm_bf16.restype = i32
     L.nk_qk_norm_rope_cache_bf16.argtypes = [vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32,
-                                             i32, i32, i64, i64, i64, f32, vp]
+                                             i32, i32, i32, i64, i64, i64, f32, vp]
     L.nk_qk_norm_rope_cache_bf16.restype = i32
     L.nk_attention_ws_bytes.argtypes = [i32, i32, i32]
     L.nk_attention_ws_bytes.restype = ctypes.c_size_t

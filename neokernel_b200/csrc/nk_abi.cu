@@ -251,6 +251,7 @@ extern "C" const char* nk_status_string(int status) {
         case NK_ERR_DEVICE: return "current device is not an sm_100 (B200-class) GPU";
         case NK_ERR_TIMEOUT: return "bounded device wait expired";
         case NK_ERR_ARG: return "invalid argument";
+        case NK_ERR_RANGE: return "decode position outside the cache";
         default: return "unknown status";
     }
 }

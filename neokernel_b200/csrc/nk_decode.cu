@@ -124,7 +124,8 @@ qk_norm_rope_cache_kernel(const __nv_bfloat16* qkv, int64_t ld_qkv, const __nv_b
                           const __nv_bfloat16* kn, const __nv_bfloat16* cos_t,
                           const __nv_bfloat16* sin_t, const int64_t* position,
                           __nv_bfloat16* q_out, __nv_bfloat16* k_cache, __nv_bfloat16* v_cache,
-                          int Hq, int Hkv, int64_t cb, int64_t ch, int64_t cs, float eps) {
+                          int Hq, int Hkv, int capacity, int64_t cb, int64_t ch, int64_t cs,
+                          float eps) {
     __shared__ float red[32];
     __shared__ float xs[kHeadDim];
     if (threadIdx.x == 0) griddep_launch_dependents();
@@ -133,6 +134,10 @@ qk_norm_rope_cache_kernel(const __nv_bfloat16* qkv, int64_t ld_qkv, const __nv_b
     const int b = blockIdx.y;
     const int d = threadIdx.x;
     const int64_t pos = *position;
+    if (pos < 0 || pos >= capacity) {  // no cache slot (and no RoPE row) to use
+        if (h == 0 && b == 0 && d == 0) atomicExch(&g_error, NK_ERR_RANGE);
+        return;
+    }
     const bool is_q = h < Hq;
     const __nv_bfloat16* src = qkv + (int64_t)b * ld_qkv + (int64_t)h * kHeadDim;
     const float x = __bfloat162float(src[d]);
@@ -263,9 +268,12 @@ attn_partial_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
     griddep_wait();
     const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t pos = min(*position, (int64_t)capacity - 1);  // never past the cache
+    const int64_t pos_in = *position;
+    const int64_t pos = min(pos_in, (int64_t)capacity - 1);  // never past the cache
+    if ((pos_in < 0 || pos_in >= capacity) && split == 0 && kh == 0 && b == 0 && threadIdx.x == 0)
+        atomicExch(&g_error, NK_ERR_RANGE);
     const int j0 = split * kAttnChunk;
-    if ((int64_t)j0 > pos) return;
+    if ((int64_t)j0 > pos) return;  // also every CTA when the position is negative
     const int valid = (int)min((int64_t)kAttnChunk, pos + 1 - j0);
 
     const uint32_t sk = smem_u32(s_tiles), sv = sk + kAttnTileBytes;
@@ -407,6 +415,7 @@ attn_merge_kernel(const float* part_acc, const float* part_ml, __nv_bfloat16* ou
     const int64_t hrow = blockIdx.x;  // b * Hq + h
     const int d = threadIdx.x;
     const int64_t pos = min(*position, (int64_t)capacity - 1);
+    if (pos < 0) return;  // no partials were written (the partial kernel flagged it)
     const int used = (int)min((int64_t)splits, pos / kAttnChunk + 1);
     const float* ml = part_ml + hrow * splits * 2;
     const float* pa = part_acc + hrow * splits * kHeadDim + d;
@@ -483,14 +492,14 @@ extern "C" int nk_qk_norm_rope_cache_bf16(const void* qkv, int64_t ld_qkv, const
                                           const void* k_norm, const void* cos_table,
                                           const void* sin_table, const int64_t* position,
                                           void* q_out, void* k_cache, void* v_cache, int batch,
-                                          int q_heads, int kv_heads, int head_dim,
+                                          int q_heads, int kv_heads, int head_dim, int capacity,
                                           int64_t cache_batch_stride, int64_t cache_head_stride,
                                           int64_t cache_seq_stride, float eps,
                                           nk_stream_t stream) {
     if (!qkv || !q_norm || !k_norm || !cos_table || !sin_table || !position || !q_out ||
         !k_cache || !v_cache)
         return NK_ERR_ARG;
-    if (head_dim != kHeadDim || batch < 1 || q_heads < 1 || kv_heads < 1 ||
+    if (head_dim != kHeadDim || batch < 1 || q_heads < 1 || kv_heads < 1 || capacity < 1 ||
         ld_qkv < (int64_t)(q_heads + 2 * kv_heads) * head_dim || cache_seq_stride < head_dim)
         return NK_ERR_SHAPE;
     return launch_pdl_smem(
@@ -499,7 +508,7 @@ extern "C" int nk_qk_norm_rope_cache_bf16(const void* qkv, int64_t ld_qkv, const
         static_cast<const __nv_bfloat16*>(q_norm), static_cast<const __nv_bfloat16*>(k_norm),
         static_cast<const __nv_bfloat16*>(cos_table), static_cast<const __nv_bfloat16*>(sin_table),
         position, static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
-        static_cast<__nv_bfloat16*>(v_cache), q_heads, kv_heads, cache_batch_stride,
+        static_cast<__nv_bfloat16*>(v_cache), q_heads, kv_heads, capacity, cache_batch_stride,
         cache_head_stride, cache_seq_stride, eps);
 }
 

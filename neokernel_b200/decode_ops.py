@@ -58,7 +58,8 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, eps: float
 def qk_norm_rope_cache(qkv, q_norm, k_norm, cos, sin, position, q_out, k_cache, v_cache,
                        heads: int, kv_heads: int, eps: float):
     """Q/K head RMSNorm + RoPE at ``position`` (device int64 [1]); queries to ``q_out``
-    [B, heads*128], keys and values into the [B, kv_heads, capacity, 128] caches."""
+    [B, heads*128], keys and values into the [B, kv_heads, capacity, 128] caches. A position
+    outside the caches writes nothing and is reported by ``device_error()``."""
     _bf16_cuda(qkv, q_norm, k_norm, cos, sin, q_out, k_cache, v_cache)
     _need(position.is_cuda and position.dtype == torch.int64, "position: CUDA int64 tensor")
     B = qkv.shape[0]
@@ -68,8 +69,8 @@ def qk_norm_rope_cache(qkv, q_norm, k_norm, cos, sin, position, q_out, k_cache, 
     st = _lib.load().nk_qk_norm_rope_cache_bf16(
         qkv.data_ptr(), qkv.stride(0), q_norm.data_ptr(), k_norm.data_ptr(), cos.data_ptr(),
         sin.data_ptr(), position.data_ptr(), q_out.data_ptr(), k_cache.data_ptr(),
-        v_cache.data_ptr(), B, heads, kv_heads, HEAD_DIM, k_cache.stride(0), k_cache.stride(1),
-        k_cache.stride(2), float(eps), _stream(qkv))
+        v_cache.data_ptr(), B, heads, kv_heads, HEAD_DIM, k_cache.shape[2], k_cache.stride(0),
+        k_cache.stride(1), k_cache.stride(2), float(eps), _stream(qkv))
     if st != _lib.NK_OK:
         _raise(st, "nk_qk_norm_rope_cache_bf16")
 

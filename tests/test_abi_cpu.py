@@ -34,7 +34,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_status_strings_distinct():
-    codes = [0, -1, -2, -3, -4, -5, -6, -7, -8, -9]
+    codes = [0, -1, -2, -3, -4, -5, -6, -7, -8, -9, -10]
     texts = [_lib.status_string(c) for c in codes]
     assert len(set(texts)) == len(codes)
     assert _lib.status_string(-99) == "unknown status"

@@ -149,7 +149,11 @@ def test_attention_decode_8_byte_aligned_cache(H, Hkv):
 
 
 def test_attention_decode_position_clamped_to_capacity():
-    """A position past the cache attends over the whole cache, reading nothing beyond it."""
+    """A position past the cache attends over the whole cache, reading nothing beyond it, and
+    is reported; a negative one writes nothing."""
+    import neokernel_b200 as nk
+    from neokernel_b200 import _lib
+    assert nk.device_error() == 0
     B, H, Hkv, cap = 2, 32, 8, 100
     kc = rand(B, Hkv, cap, 128, seed=13)
     vc = rand(B, Hkv, cap, 128, seed=14)
@@ -157,9 +161,35 @@ def test_attention_decode_position_clamped_to_capacity():
     q = rand(B, H * 128, seed=15)
     a, b = torch.empty_like(q), torch.empty_like(q)
     ops.attention_decode(q, kc, vc, torch.tensor([cap - 1], device=DEV), a, ws, H, Hkv)
+    assert nk.device_error() == 0
     ops.attention_decode(q, kc, vc, torch.tensor([cap + 37], device=DEV), b, ws, H, Hkv)
-    torch.cuda.synchronize()
+    assert nk.device_error() == _lib.NK_ERR_RANGE
     assert torch.equal(a, b)
+    c = torch.full_like(q, 7.0)
+    ops.attention_decode(q, kc, vc, torch.tensor([-1], device=DEV), c, ws, H, Hkv)
+    assert nk.device_error() == _lib.NK_ERR_RANGE
+    assert (c.float() == 7.0).all()
+
+
+@pytest.mark.parametrize("pos_off", (0, 5))
+def test_qk_norm_rope_cache_position_outside_cache(pos_off):
+    """A position at or past the capacity (or negative) writes nothing and is reported."""
+    import neokernel_b200 as nk
+    from neokernel_b200 import _lib
+    B, H, Hkv, cap = 2, 32, 8, 40
+    d = qwen3.Qwen3Dims(1024, 1024, H, Hkv, 128, 1, 64)
+    cos, sin = qwen3.rope_tables(d, cap, DEV)
+    qn, kn = rand(128, seed=4), rand(128, seed=5)
+    qkv = rand(B, (H + 2 * Hkv) * 128, seed=6)
+    kc = torch.zeros(B, Hkv, cap, 128, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    q_out = torch.full((B, H * 128), 3.0, dtype=torch.bfloat16, device=DEV)
+    for pos in (cap + pos_off, -1 - pos_off):
+        ops.qk_norm_rope_cache(qkv, qn, kn, cos, sin, torch.tensor([pos], device=DEV), q_out,
+                               kc, vc, H, Hkv, 1e-6)
+        assert nk.device_error() == _lib.NK_ERR_RANGE
+    assert kc.count_nonzero().item() == 0 and vc.count_nonzero().item() == 0
+    assert (q_out.float() == 3.0).all()
 
 
 @pytest.mark.parametrize("rows", (1, 16))
