@@ -92,6 +92,24 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// Weight-tile load marked evict-first in L2: every weight byte is read once per decode step,
+// so these lines should be the first to leave and not push out the activations, partials and
+// KV rows that are read again.
+__device__ __forceinline__ void tma_load_w(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                           int c0, int c1, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -289,6 +307,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
         if (lane == 0) {
             // ---------------- TMA producer ----------------
             const int n_pre = n_units < STAGES ? n_units : STAGES;
+            const uint64_t wpol = l2_evict_first_policy();
             // The first stages' weight tiles need nothing from the previous kernel.
             for (int i = 0; i < n_pre; ++i) {
                 const int64_t u = u_begin + i;
@@ -297,8 +316,8 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                 mbar_expect_tx(bar_full + 8 * i, (uint32_t)L::kStage);
 #pragma unroll
                 for (int ub = 0; ub < kTcUK; ++ub)
-                    tma_load_2d(base + i * L::kStage + ub * L::kBoxA, &tmap_w, bar_full + 8 * i,
-                                kb * kTcKStep + ub * kTcBox, (t % a.n_tiles) * kTcRows);
+                    tma_load_w(base + i * L::kStage + ub * L::kBoxA, &tmap_w, bar_full + 8 * i,
+                               kb * kTcKStep + ub * kTcBox, (t % a.n_tiles) * kTcRows, wpol);
             }
             griddep_wait();
             for (int i = 0; i < n_pre; ++i) {
@@ -323,8 +342,8 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                 mbar_expect_tx(bar_full + 8 * st, (uint32_t)L::kStage);
 #pragma unroll
                 for (int ub = 0; ub < kTcUK; ++ub)
-                    tma_load_2d(sa + ub * L::kBoxA, &tmap_w, bar_full + 8 * st,
-                                kb * kTcKStep + ub * kTcBox, (t % a.n_tiles) * kTcRows);
+                    tma_load_w(sa + ub * L::kBoxA, &tmap_w, bar_full + 8 * st,
+                               kb * kTcKStep + ub * kTcBox, (t % a.n_tiles) * kTcRows, wpol);
 #pragma unroll
                 for (int ub = 0; ub < kTcUK; ++ub)
                     tma_load_2d(sa + L::kA + ub * L::kBoxB, &tmap_x, bar_full + 8 * st,
