@@ -68,57 +68,113 @@ def step_bytes(m_list):
 # clocks sampled with nvidia-smi during the timed region
 # ---------------------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock and clock-event (throttle) reasons of one GPU, sampled every 10 ms by an NVML
+    thread while the timed region runs (read-only queries; nothing is set). Without NVML it
+    falls back to ``nvidia-smi -lms 200``."""
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown", 0x8),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap", 0x4))
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.path = None
+    def __init__(self, device_index: int, period_s: float = 0.01):
+        self.dev = device_index
+        self.period = period_s
+        self.rows = []          # (sm_mhz, reason bitmask)
+        self.max_mhz = None
+        self.source = None
+        self._stop = None
+        self._thread = None
+        self._proc = None
+        self._path = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:   # the CUDA device's PCI address names the same GPU under any device ordering
+            pr = torch.cuda.get_device_properties(self.dev)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.dev)
 
     def __enter__(self):
-        fd, self.path = tempfile.mkstemp(suffix=".csv")
-        os.close(fd)
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            nv, h = self._nvml_handle()
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons",
+                                  getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+            self._stop = threading.Event()
+
+            def run():
+                while True:
+                    try:
+                        self.rows.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                          int(get_reasons(h))))
+                    except Exception:
+                        pass
+                    if self._stop.wait(self.period):
+                        break
+            self._thread = threading.Thread(target=run, daemon=True)
+            self._thread.start()
+            self.source = f"nvml every {int(self.period * 1000)} ms"
         except Exception:
-            self.proc = None
+            fd, self._path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            try:
+                self._proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.QUERY}",
+                     "--format=csv,noheader,nounits", "-lms", "200"],
+                    stdout=open(self._path, "w"), stderr=subprocess.DEVNULL)
+                self.source = "nvidia-smi -lms 200"
+            except Exception:
+                self._proc = None
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+        if self._proc is not None:
+            self._proc.terminate()
             try:
-                self.proc.wait(timeout=5)
+                self._proc.wait(timeout=5)
             except Exception:
-                self.proc.kill()
+                self._proc.kill()
 
     def summary(self):
-        rows = []
-        try:
-            for line in open(self.path):
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
-        except Exception:
-            pass
-        finally:
+        names = [n for n, _, _ in self.REASONS]
+        if self._path is not None:  # nvidia-smi rows
             try:
-                os.unlink(self.path)
+                for line in open(self._path):
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                        mask = sum(bit for i, (_, _, bit) in enumerate(self.REASONS)
+                                   if parts[5 + i] == "Active")
+                        self.rows.append((float(parts[1]), mask))
+                        if parts[2].replace(".", "").isdigit():
+                            self.max_mhz = max(self.max_mhz or 0.0, float(parts[2]))
             except Exception:
                 pass
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+            finally:
+                try:
+                    os.unlink(self._path)
+                except Exception:
+                    pass
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"],
+                    "samples": 0, "source": self.source}
+        try:
+            import pynvml as nv
+            bits = [getattr(nv, attr, bit) for _, attr, bit in self.REASONS]
+        except Exception:
+            bits = [bit for _, _, bit in self.REASONS]
+        reasons = sorted({names[i] for _, m in self.rows for i in range(4) if m & bits[i]})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.rows), "source": self.source}
 
 
 # ---------------------------------------------------------------------------------------
@@ -251,6 +307,9 @@ def main():
     ap.add_argument("--single", default=None,
                     help="N,K,M: run one decode linear --reps times and exit (profiler captures)")
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--attention", default=None,
+                    help="B,KV: run --reps Qwen3-8B decode-attention launches (32 query / 8 KV "
+                         "heads, synthetic cache of KV positions) on cuda:0 and exit")
     ap.add_argument("--decode-step", type=int, default=0,
                     help="B: run --reps fused Qwen3-8B decode steps at batch B, KV 1024, and exit "
                          "(profiler captures of the whole step)")
@@ -259,6 +318,8 @@ def main():
         return reference_arm(args)
     if args.single:
         return single(args)
+    if args.attention:
+        return attention_only(args)
     if args.decode_step:
         return decode_step_only(args)
     if args.warmup < 3:
@@ -485,6 +546,29 @@ def single(args):
         nk.mm(x, W.t(), out=y, plan=plan)
     torch.cuda.synchronize(dev)
     print(json.dumps({"single": [N, K, M], "reps": args.reps, "plan": plan.as_dict()}))
+    return 0
+
+
+def attention_only(args):
+    """--reps launches of one Qwen3-8B layer's decode attention (32 query heads over 8 KV heads
+    of 128) at batch B with KV positions cached (a small, self-contained case for ncu)."""
+    from neokernel_b200 import decode_ops as ops
+    from neokernel_b200 import synthetic
+    B, kv = (int(v) for v in args.attention.split(","))
+    dev = torch.device("cuda", 0)
+    H, Hkv, D = 32, 8, 128
+    cap = kv + 1
+    kc = synthetic.activation(B * Hkv * cap, D, seed=3, device=dev).view(B, Hkv, cap, D)
+    vc = synthetic.activation(B * Hkv * cap, D, seed=4, device=dev).view(B, Hkv, cap, D)
+    q = synthetic.activation(B, H * D, seed=5, device=dev)
+    out = torch.empty_like(q)
+    ws = ops.attention_workspace(B, H, cap, dev)
+    position = torch.tensor([kv], device=dev)
+    for _ in range(args.reps):
+        ops.attention_decode(q, kc, vc, position, out, ws, H, Hkv)
+    torch.cuda.synchronize(dev)
+    kv_bytes = 2 * B * Hkv * (kv + 1) * D * 2
+    print(json.dumps({"attention": [B, kv], "reps": args.reps, "kv_bytes": kv_bytes}))
     return 0
 
 
