@@ -106,7 +106,9 @@ NK_API int nk_plan_make(nk_plan* plan, int M_max, int N, int K, int split_k, int
  * tiles are refused (NK_ERR_SPLIT). */
 NK_API size_t nk_ws_bytes(const nk_plan* plan);
 
-/* Zero a workspace once before its first use (the kernels keep it zeroed afterwards).
+/* Zero a workspace once before its first use (the kernels keep it zeroed afterwards). After
+ * nk_device_error has reported NK_ERR_TIMEOUT, zero it again: a launch that stopped on an
+ * expired wait may have left split-K state behind.
  * Asynchronous on `stream`. */
 NK_API int nk_ws_init(void* ws, size_t ws_bytes, nk_stream_t stream);
 

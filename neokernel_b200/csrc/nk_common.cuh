@@ -160,10 +160,11 @@ inline WsLayout ws_layout(const nk_plan& p) {
     L.ticket_count = (size_t)p.n_tiles * (size_t)p.m_tiles;
     L.part_offset = kTicketBytes;
     if (p.kind == NK_KIND_TC) {
-        // [tile][segment][token column][128 rows] fp32, only when some tile is shared
+        // [tile][segment][token column][128 rows] 64-bit {fp32 value, tag} slots, only when
+        // some tile is shared
         if (p.segments <= 1) return WsLayout{};
         const size_t cols = (size_t)(p.M_max < p.tile_m ? p.M_max : p.tile_m);
-        L.part_bytes = L.ticket_count * (size_t)p.segments * cols * 128 * sizeof(float);
+        L.part_bytes = L.ticket_count * (size_t)p.segments * cols * 128 * sizeof(uint64_t);
     } else {
         // [slice][M][N] fp32
         if (p.split_k <= 1) return WsLayout{};

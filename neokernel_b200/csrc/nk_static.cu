@@ -64,9 +64,9 @@ extern "C" int nk_gemm_bf16_static(const void* x, int64_t ldx, const void* w, in
     void* scratch = nullptr;
     const int st = static_scratch_address(&scratch);
     if (st != NK_OK) return st;
-    // The tickets must start at zero; the previous call may have left any value in them.
-    if (cudaMemsetAsync(scratch, 0, L.ticket_count * sizeof(unsigned), (cudaStream_t)stream) !=
-        cudaSuccess)
+    // Tickets and partial slots must start at zero; every call leaves them so, but one that
+    // stopped on an expired wait may not have, and the array is shared by all plans.
+    if (cudaMemsetAsync(scratch, 0, L.total, (cudaStream_t)stream) != cudaSuccess)
         return NK_ERR_CUDA;
     return nk_gemm_bf16(x, ldx, w, ldw, y, ldy, M, N, K, plan, scratch,
                         (size_t)NK_STATIC_SCRATCH_BYTES, stream);

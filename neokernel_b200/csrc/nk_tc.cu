@@ -226,6 +226,103 @@ struct TcSmem {
     static_assert(kBoxB % 1024 == 0, "activation boxes must keep 1 KB swizzle-atom alignment");
 };
 
+// Partials of shared tiles. For decode-sized launches (M <= NK_TC_TAG_MAX_M) they live in
+// 64-bit slots {fp32 value, tag}: a rank publishes a value and its tag in one store, so a
+// reader that sees the tag has the value without a fence, a count or a second round trip, and
+// the reader clears the slot after use. The tag is a signalling-NaN bit pattern, which no
+// arithmetic produces, so no value left by another plan, launch or kernel family can pose as
+// a published slot. Larger launches, whose partials would need many slot rounds, publish
+// plain fp32 followed by a fence and the tile's count.
+#ifndef NK_TC_TAG_MAX_M
+#define NK_TC_TAG_MAX_M 8
+#endif
+constexpr uint32_t kSlotTag = 0x7FBADC0Du;
+
+__device__ __forceinline__ void st_slot(uint64_t* p, float v) {
+    const uint64_t x = ((uint64_t)kSlotTag << 32) | (uint64_t)__float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(x) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_slot(const uint64_t* p) {
+    uint64_t x;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(x) : "l"(p) : "memory");
+    return x;
+}
+
+__device__ __forceinline__ void clear_slot(uint64_t* p) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"((uint64_t)0) : "memory");
+}
+
+// ps[j] += the plain fp32 partials of ranks 1, 2, ..., nseg-1 (in that order) at token
+// columns c0 + j < mcount of one tile row (part0: the row's rank-0, column-0 value); the caller
+// has seen the tile's count complete.
+__device__ __forceinline__ void sum_partials16(const float* part0, int part_cols, int c0,
+                                               int nseg, int mcount, float (&ps)[16]) {
+#pragma unroll 2
+    for (int r = 1; r < nseg; ++r) {
+        const float* pr = part0 + ((size_t)r * part_cols + c0) * kTcRows;
+        float p[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            p[j] = (c0 + j < mcount) ? __ldcg(pr + (size_t)j * kTcRows) : 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) ps[j] += p[j];
+    }
+}
+
+// ps[j] += the partials of ranks 1, 2, ..., nseg-1 (in that order) at token columns
+// c0 + j < mcount of one tile row (slot0: the row's rank-0, column-0 slot), clearing each
+// slot it reads. Slots are read four ranks x four columns at a time; while some are not yet
+// published, all of those are read again together (one L2 round trip per round), bounded by
+// ~2 s (then NK_ERR_TIMEOUT is recorded and false returned).
+__device__ __forceinline__ bool collect_partials16(uint64_t* slot0, int part_cols, int c0,
+                                                   int nseg, int mcount, float (&ps)[16]) {
+    for (int r0 = 1; r0 < nseg; r0 += 4) {
+#pragma unroll
+        for (int j0 = 0; j0 < 16; j0 += 4) {
+            if (c0 + j0 >= mcount) break;
+            uint64_t x[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    x[i][j] = (r0 + i < nseg && c0 + j0 + j < mcount)
+                                  ? ld_slot(slot0 + ((size_t)(r0 + i) * part_cols + c0 + j0 + j) * kTcRows)
+                                  : ((uint64_t)kSlotTag << 32);
+            uint64_t t0 = 0;
+            for (;;) {
+                bool all = true;
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) all &= (uint32_t)(x[i][j] >> 32) == kSlotTag;
+                if (all) break;
+                if (t0 == 0) t0 = global_ns();
+                if (global_ns() - t0 > 2000000000ull) {
+                    atomicExch(&g_error, NK_ERR_TIMEOUT);
+                    return false;
+                }
+                __nanosleep(32);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if ((uint32_t)(x[i][j] >> 32) != kSlotTag)
+                            x[i][j] = ld_slot(slot0 + ((size_t)(r0 + i) * part_cols + c0 + j0 + j) * kTcRows);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (r0 + i < nseg && c0 + j0 + j < mcount) {
+                        ps[j0 + j] += __uint_as_float((uint32_t)x[i][j]);
+                        clear_slot(slot0 + ((size_t)(r0 + i) * part_cols + c0 + j0 + j) * kTcRows);
+                    }
+        }
+    }
+    return true;
+}
+
 // One tile segment of this CTA's unit range.
 struct Segment {
     int t;         // tile index
@@ -400,6 +497,8 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
         const int q = warp & 3;                   // TMEM lane quarter this warp may access
         const int row = 32 * q + lane;            // tile row owned by this thread
         const uint32_t tlane = (uint32_t)(32 * q) << 16;
+        const bool wait_mode = a.coresident != 0;
+        const bool tagged = wait_mode && a.M <= NK_TC_TAG_MAX_M;  // the same for every CTA
         int seg = 0;
         for (int64_t u = u_begin; u < u_end; ++seg) {
             const Segment sg = segment_at(u, u_end, KB);
@@ -409,66 +508,53 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             const int m0 = (sg.t / a.n_tiles) * NT;
             const int mcount = min(NT, a.M - m0);
             const bool whole = (sg.kb0 == 0 && sg.kb1 == KB);
-            const bool ok = mbar_wait(bar_tfull + 8 * buf, (uint32_t)(seg >> 1) & 1u) &&
-                            *abort_flag == 0u;
-            tc_fence_after();
-            const uint32_t taddr = tmem + (uint32_t)(buf * NT) + tlane;
             const int first = P.first_cta(sg.t);
             const int rank = c - first;
             const int nseg = whole ? 1 : P.last_cta(sg.t) - first + 1;
-            float* slot0 = a.part + ((size_t)sg.t * a.segments * a.part_cols) * kTcRows + row;
-            const bool wait_mode = a.coresident != 0;
-            if (whole || rank > 0 || !wait_mode) {
-                // Whole tile: bf16 out. Rank >= 1 of a shared tile (always this CTA's first
-                // segment): publish the fp32 partial for the tile's rank-0 CTA. Without a
-                // co-resident grid every rank publishes and the last to arrive sums them.
-                float* dst = slot0 + (size_t)rank * a.part_cols * kTcRows;
+            // This row's partials of the tile, [rank][token column], 128 rows apart: 64-bit
+            // tagged slots, or plain fp32 in the same region.
+            const size_t row0 = ((size_t)sg.t * a.segments * a.part_cols) * kTcRows + row;
+            uint64_t* const slot0 = reinterpret_cast<uint64_t*>(a.part) + row0;
+            float* const part0 = a.part + row0;
+            const bool finisher = !whole && rank == 0 && wait_mode;
+            // Rank 0 of a shared tile holds the tile's first K blocks as its last segment; the
+            // other ranks (higher CTAs) hold the rest. It waits for them while its own last
+            // MMAs still run and, for the decode token tile, already adds up their partials
+            // (rank 1 + rank 2 + ...), so that once its accumulator is ready only own + that
+            // sum is left.
+            float psum[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) psum[j] = 0.f;
+            bool got = true;
+            if (finisher && !tagged) {
+                if (ep == 0)
+                    *last_flag = spin_until_count(a.tickets + sg.t, (unsigned)(nseg - 1)) ? 1u : 0u;
+                epi_bar();
+                __threadfence();
+                got = *last_flag != 0u;
+            }
+            if constexpr (NT == 16) {
+                if (finisher) {
+                    if (tagged) got = collect_partials16(slot0, a.part_cols, 0, nseg, mcount, psum);
+                    else if (got) sum_partials16(part0, a.part_cols, 0, nseg, mcount, psum);
+                }
+                __syncwarp();  // lanes polled for different times; converge before tcgen05.ld
+            }
+            // warp-uniform (and a convergence point) before the warp-wide tcgen05.ld below
+            const bool ok = __all_sync(0xffffffffu,
+                                       mbar_wait(bar_tfull + 8 * buf, (uint32_t)(seg >> 1) & 1u) &&
+                                           *abort_flag == 0u);
+            tc_fence_after();
+            const uint32_t taddr = tmem + (uint32_t)(buf * NT) + tlane;
+            // tcgen05.ld is a warp-wide instruction: every lane of the warp executes it, and
+            // only the stores depend on the lane's row (n < N) or on what it collected.
+            if (whole) {
                 if (ok) {
 #pragma unroll 1
                     for (int c0 = 0; c0 < NT; c0 += 16) {
                         if (c0 >= mcount) break;  // warp-uniform
                         float v[16];
                         tmem_ld16(taddr + c0, v);
-                        if (whole) {
-                            if (n < a.N) {
-#pragma unroll
-                                for (int j = 0; j < 16; ++j)
-                                    if (c0 + j < mcount)
-                                        store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n, v[j]);
-                            }
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 16; ++j)
-                                if (c0 + j < mcount) dst[(size_t)(c0 + j) * kTcRows] = v[j];
-                        }
-                    }
-                }
-            } else {
-                // Rank 0 of a shared tile: it holds the tile's first K blocks and this is its
-                // last segment, so the other ranks (higher CTAs, whose share is their first
-                // segment) have published long ago. Wait (bounded) for their count, then sum
-                // own + rank 1 + rank 2 ... — ascending k, the same order whoever is late.
-                if (ep == 0) {
-                    *last_flag = spin_until_count(a.tickets + sg.t, (unsigned)(nseg - 1)) ? 1u : 0u;
-                }
-                epi_bar();
-                __threadfence();
-                if (ok && *last_flag) {
-#pragma unroll 1
-                    for (int c0 = 0; c0 < NT; c0 += 16) {
-                        if (c0 >= mcount) break;  // warp-uniform
-                        float v[16];
-                        tmem_ld16(taddr + c0, v);
-#pragma unroll 2
-                        for (int r = 1; r < nseg; ++r) {
-                            const float* pr = slot0 + ((size_t)r * a.part_cols + c0) * kTcRows;
-                            float p[16];
-#pragma unroll
-                            for (int j = 0; j < 16; ++j)
-                                p[j] = (c0 + j < mcount) ? __ldcg(pr + (size_t)j * kTcRows) : 0.f;
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) v[j] += p[j];
-                        }
                         if (n < a.N) {
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
@@ -477,18 +563,61 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                         }
                     }
                 }
-                if (ep == 0) a.tickets[sg.t] = 0u;  // re-armed for the next launch
+            } else if (!finisher) {
+                // Publish this rank's fp32 partial: as tagged slots (a value and its tag in one
+                // 64-bit store, so no fence or count follows), or as plain fp32 followed below
+                // by a fence and the tile's count.
+                if (ok) {
+#pragma unroll 1
+                    for (int c0 = 0; c0 < NT; c0 += 16) {
+                        if (c0 >= mcount) break;  // warp-uniform
+                        float v[16];
+                        tmem_ld16(taddr + c0, v);
+                        const size_t off = ((size_t)rank * a.part_cols + c0) * kTcRows;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (c0 + j < mcount) {
+                                if (tagged) st_slot(slot0 + off + (size_t)j * kTcRows, v[j]);
+                                else part0[off + (size_t)j * kTcRows] = v[j];
+                            }
+                    }
+                }
+            } else {
+                // own + (rank 1 + rank 2 + ...): a fixed order, whichever rank is late
+                if (ok) {
+#pragma unroll 1
+                    for (int c0 = 0; c0 < NT; c0 += 16) {
+                        if (c0 >= mcount) break;  // warp-uniform
+                        if constexpr (NT != 16) {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) psum[j] = 0.f;
+                            if (tagged) got = collect_partials16(slot0, a.part_cols, c0, nseg, mcount, psum);
+                            else if (got) sum_partials16(part0, a.part_cols, c0, nseg, mcount, psum);
+                            __syncwarp();  // converge before tcgen05.ld
+                        }
+                        float v[16];
+                        tmem_ld16(taddr + c0, v);
+                        if (got && n < a.N) {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                if (c0 + j < mcount)
+                                    store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n, v[j] + psum[j]);
+                        }
+                    }
+                }
+                if (!tagged && ep == 0) a.tickets[sg.t] = 0u;  // re-armed for the next launch
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_tempty + 8 * buf);
-            if (!whole && wait_mode && rank > 0) {
+            if (!whole && wait_mode && !tagged && rank > 0) {
                 __threadfence();  // this CTA's partial stores, before the count that publishes them
                 epi_bar();
                 if (ep == 0) atomicAdd(a.tickets + sg.t, 1u);
             } else if (!whole && !wait_mode) {
-                // No waiting: the CTA whose count completes the tile sums every rank's
-                // partial in ascending rank order (the same order as the waiting scheme).
+                // Without a co-resident grid every rank publishes plain partials (rank 0 above as
+                // well) and the CTA whose arrival completes the tile's count sums them, in the
+                // same order as the waiting scheme: rank 0 + (rank 1 + rank 2 + ...).
                 __threadfence();
                 epi_bar();
                 if (ep == 0) {
@@ -500,26 +629,18 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                     __threadfence();
                     if (n < a.N && *abort_flag == 0u) {
                         for (int c0 = 0; c0 < mcount; c0 += 16) {
-                            float v[16];
+                            float ps[16];
 #pragma unroll
-                            for (int j = 0; j < 16; ++j) v[j] = 0.f;
-#pragma unroll 2
-                            for (int r = 0; r < nseg; ++r) {
-                                const float* pr = slot0 + ((size_t)r * a.part_cols + c0) * kTcRows;
-                                float p[16];
-#pragma unroll
-                                for (int j = 0; j < 16; ++j)
-                                    p[j] = (c0 + j < mcount) ? __ldcg(pr + (size_t)j * kTcRows) : 0.f;
-#pragma unroll
-                                for (int j = 0; j < 16; ++j) v[j] += p[j];
-                            }
+                            for (int j = 0; j < 16; ++j) ps[j] = 0.f;
+                            sum_partials16(part0, a.part_cols, c0, nseg, mcount, ps);
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
                                 if (c0 + j < mcount)
-                                    store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n, v[j]);
+                                    store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n,
+                                              __ldcg(part0 + ((size_t)c0 + j) * kTcRows) + ps[j]);
                         }
                     }
-                    if (ep == 0) a.tickets[sg.t] = 0u;
+                    if (ep == 0) a.tickets[sg.t] = 0u;  // re-armed for the next launch
                 }
                 epi_bar();  // last_flag is rewritten by the next partial segment
             }

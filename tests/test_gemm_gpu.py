@@ -249,6 +249,29 @@ def test_deterministic_across_runs():
             assert torch.equal(a, b)
 
 
+def test_split_protocols_share_one_workspace():
+    """Shared tiles are finished three ways: tagged partial slots (M <= 8), plain partials
+    with a fence and a count (larger M), and, when a forced split makes the grid larger than
+    can be resident, every rank publishing and the last arrival summing. Interleaved on one
+    stream's workspace, none may leave state that changes another's result."""
+    N, K = 4096, 4096
+    W = weight_dev(N, K, seed=77)
+    cases = [(1, 0), (16, 0), (4, 10), (8, 0), (3, 0), (12, 0)]
+    xs = {M: synthetic.activation(M, K, seed=300 + M, device=DEV) for M, _ in cases}
+    plans = {(M, s): nk.plan_for(M, N, K, split_k=s) for M, s in cases}
+    assert plans[(4, 10)].grid > 148 * 2  # forced split: not co-resident, no-wait finishing
+    first = {}
+    for _ in range(3):
+        for M, s in cases:
+            y = run(xs[M], W, plans[(M, s)])
+            assert (y.float() - fp32_ref(xs[M], W)).abs().max().item() <= oracle.tolerance(K)
+            if (M, s) in first:
+                assert torch.equal(y, first[(M, s)]), (M, s)
+            else:
+                first[(M, s)] = y
+    assert nk.device_error() == 0
+
+
 def test_cuda_graph_capture_and_replay():
     """Decode-style capture: side-stream warm-up x3, then capture (engine/engine.py:119-129)."""
     shapes = [(4096, 1024), (1024, 2048), (6144, 1024), (1024, 3072)] * 3 + [(151936, 1024)]
