@@ -307,6 +307,9 @@ def main():
     ap.add_argument("--single", default=None,
                     help="N,K,M: run one decode linear --reps times and exit (profiler captures)")
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--shapes", action="store_true",
+                    help="per-shape table: every Qwen3-8B (M 1..16, verify 64..256) and Qwen3-0.6B "
+                         "(M 1..16) decode linear chained 20x in a graph, weights rotated beyond L2")
     ap.add_argument("--attention", default=None,
                     help="B,KV: run --reps Qwen3-8B decode-attention launches (32 query / 8 KV "
                          "heads, synthetic cache of KV positions) on cuda:0 and exit")
@@ -320,6 +323,8 @@ def main():
         return single(args)
     if args.attention:
         return attention_only(args)
+    if args.shapes:
+        return shapes_table(args)
     if args.decode_step:
         return decode_step_only(args)
     if args.warmup < 3:
@@ -546,6 +551,77 @@ def single(args):
         nk.mm(x, W.t(), out=y, plan=plan)
     torch.cuda.synchronize(dev)
     print(json.dumps({"single": [N, K, M], "reps": args.reps, "plan": plan.as_dict()}))
+    return 0
+
+
+QWEN3_0_6B_LINEARS = [("qkv", 4096, 1024), ("o_proj", 1024, 2048), ("gate_up", 6144, 1024),
+                      ("down", 1024, 3072), ("lm_head", VOCAB, 1024)]
+
+
+def shapes_table(args, reps=5, chain=20):
+    """Per-shape decode-GEMM throughput as a decode step sees it: each (shape, M) launched
+    `chain` times in one CUDA graph (programmatic dependent launch between neighbours) with
+    its weight rotated over copies larger than 2 x L2, so every launch reads its weight from
+    DRAM. Prints one JSON line: us per launch, TB/s and the fraction of the measured HBM peak;
+    for the verify batches also TFLOP/s against the measured bf16 peak."""
+    import neokernel_b200 as nk
+    from neokernel_b200 import synthetic
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        peaks = {}
+    hbm = float(peaks.get("hbm_gbs", 6650.0)) * 1e9
+    tflops = float(peaks.get("bf16_tflops", 1590.0)) * 1e12
+    cases = [("qwen3-8b", name, N, K, M) for name, N, K in LAYER_LINEARS + [("lm_head", VOCAB, HIDDEN)]
+             for M in (1, 2, 4, 8, 16)]
+    cases += [("qwen3-8b verify", name, N, K, M) for name, N, K in LAYER_LINEARS for M in (64, 128, 256)]
+    cases += [("qwen3-0.6b", name, N, K, M) for name, N, K in QWEN3_0_6B_LINEARS for M in (1, 4, 8, 16)]
+    rows = []
+    stream = torch.cuda.Stream(device=dev)
+    weights = {}
+    for model, name, N, K, M in cases:
+        if (N, K) not in weights:
+            weights.clear()
+            torch.cuda.empty_cache()
+            copies = max(2, (2 * 126 * 2 ** 20) // (N * K * 2) + 2)
+            weights[(N, K)] = [synthetic.weight(N, K, seed=i, device=dev) for i in range(copies)]
+        Ws = weights[(N, K)]
+        x = synthetic.activation(M, K, seed=M, device=dev)
+        y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        plan = nk.plan_for(M, N, K)
+        with torch.cuda.stream(stream):
+            for W in Ws:
+                nk.mm(x, W.t(), out=y, plan=plan, stream=stream)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(chain):
+                nk.mm(x, Ws[i % len(Ws)].t(), out=y, plan=plan, stream=stream)
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * chain)
+        b = gemm_bytes(M, N, K)
+        row = {"model": model, "linear": name, "N": N, "K": K, "M": M, "us": round(us, 2),
+               "TB/s": round(b / (us * 1e-6) / 1e12, 3), "hbm_frac": round(b / (us * 1e-6) / hbm, 3)}
+        if M >= 64:
+            f = 2.0 * M * N * K
+            row["TFLOP/s"] = round(f / (us * 1e-6) / 1e12, 1)
+            row["tensor_frac"] = round(f / (us * 1e-6) / tflops, 3)
+        rows.append(row)
+        del g
+    print(json.dumps({"shapes": rows, "timing": f"CUDA graph of {chain} launches per shape, "
+                      f"{reps} replays, CUDA events; weights rotated over > 2 x L2",
+                      "peaks": {"hbm_gbs": hbm / 1e9, "bf16_tflops": tflops / 1e12}}))
     return 0
 
 

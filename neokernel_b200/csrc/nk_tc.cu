@@ -691,12 +691,17 @@ static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t col
     return r == CUDA_SUCCESS ? NK_OK : NK_ERR_ALIGN;
 }
 
+#ifndef NK_TC_MAX_NT
+#define NK_TC_MAX_NT 128  // widest token tile a plan may choose
+#endif
+
 int tc_token_tile(int M_max) {
-    if (M_max <= 16) return 16;
-    if (M_max <= 32) return 32;
-    if (M_max <= 64) return 64;
-    if (M_max <= 128) return 128;
-    return 256;
+    int nt = 256;
+    if (M_max <= 16) nt = 16;
+    else if (M_max <= 32) nt = 32;
+    else if (M_max <= 64) nt = 64;
+    else if (M_max <= 128) nt = 128;
+    return nt < NK_TC_MAX_NT ? nt : NK_TC_MAX_NT;
 }
 
 int tc_stages(int nt) {
