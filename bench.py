@@ -692,44 +692,54 @@ def decode_bench(nk, dev, batches, world, local, kv=1024, steps=20, warmup=3):
 
 def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, warmup=3):
     """Qwen3-32B-shaped tensor-parallel decode (64 layers, random init) over the N ranks of
-    this run: QKV/gate_up split by column, o_proj/down by K with an fp32 NCCL all-reduce,
-    lm_head by vocabulary; one CUDA graph per batch; KV length 2048. tok/s counts each
-    sequence's token once (the ranks share one model)."""
+    this run: QKV/gate_up split by column, o_proj/down by K with their fp32 partials summed
+    across ranks, lm_head by vocabulary; one CUDA graph per batch; KV length 2048. The
+    product ("auto") sums the partials with the peer-memory all-reduce (nk_allreduce_bf16) for
+    small batches and NCCL's all-reduce for large ones; at N > 1 the step with each of the two
+    throughout is timed beside it. tok/s counts each sequence's token once (the ranks share
+    one model)."""
     from neokernel_b200 import qwen3, tp
     d = qwen3.QWEN3_32B
     w = tp.TPWeights(d, seed=13, rank=rank, world=world, device=dev)
-    res = {}
-    for B in batches:
-        g = qwen3.GraphDecoder(w, B, kv + warmup + steps + 1, nk.mm, device=dev,
-                               make_hooks=tp.make_hooks(w), fused=True)
-        gen = torch.Generator(device=dev).manual_seed(100 + B)
-        for c in g.st.k_cache + g.st.v_cache:
-            c.normal_(generator=gen)
-        g.st.position.fill_(kv)
-        g.st.tokens.copy_(torch.randint(0, d.vocab, (B,), generator=torch.Generator(
-            device=dev).manual_seed(B), device=dev))  # same tokens on every rank
-        for _ in range(warmup):
-            g.step()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier(world)
-        torch.cuda.synchronize(dev)
-        a.record()
-        for _ in range(steps):
-            g.step()
-        b.record()
-        b.synchronize()
-        ms = max_over_ranks(a.elapsed_time(b), world, local) / steps
-        res[str(B)] = {"ms_per_token_step": round(ms, 3), "tok_s": round(B / (ms / 1e3), 1)}
-        barrier(world)
-        del g.graph  # NCCL-holding graph released before anything tears down the group
-        del g
-        torch.cuda.empty_cache()
+    arms = ("auto", "peer", "nccl") if world > 1 else ("auto",)
+    out = {}
+    for collective in arms:
+        res = {}
+        for B in batches:
+            g = qwen3.GraphDecoder(w, B, kv + warmup + steps + 1, nk.mm, device=dev,
+                                   make_hooks=tp.make_hooks(w, collective=collective), fused=True)
+            gen = torch.Generator(device=dev).manual_seed(100 + B)
+            for c in g.st.k_cache + g.st.v_cache:
+                c.normal_(generator=gen)
+            g.st.position.fill_(kv)
+            g.st.tokens.copy_(torch.randint(0, d.vocab, (B,), generator=torch.Generator(
+                device=dev).manual_seed(B), device=dev))  # same tokens on every rank
+            for _ in range(warmup):
+                g.step()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier(world)
+            torch.cuda.synchronize(dev)
+            a.record()
+            for _ in range(steps):
+                g.step()
+            b.record()
+            b.synchronize()
+            ms = max_over_ranks(a.elapsed_time(b), world, local) / steps
+            res[str(B)] = {"ms_per_token_step": round(ms, 3), "tok_s": round(B / (ms / 1e3), 1)}
+            barrier(world)
+            del g.graph  # NCCL-holding graph released before anything tears down the group
+            del g
+            torch.cuda.empty_cache()
+        out[collective] = res
     del w
     torch.cuda.empty_cache()
     return {"model": "qwen3-32b random-init, 64 layers, hidden 5120, MLP 25600, 64Q/8KV x 128",
-            "tp": world, "kv_length": kv, "steps": steps, "batches": res,
-            "collectives": "fp32 all-reduce after o_proj and down, all-gather of (max, index) "
-                           "for the vocab-split argmax; NCCL, captured in the CUDA graph"}
+            "tp": world, "kv_length": kv, "steps": steps, "batches": out["auto"],
+            "batches_peer_allreduce": out.get("peer"), "batches_nccl_allreduce": out.get("nccl"),
+            "collectives": "fp32 partials of o_proj and down summed across ranks, one bf16 "
+                           "rounding: nk_allreduce_bf16 over NVLink peer memory (rank order) up "
+                           "to 64K elements, NCCL all-reduce above; NCCL all-gather of (max, "
+                           "index) for the vocab-split argmax; all captured in the CUDA graph"}
 
 
 def decode_step_only(args, kv=1024):

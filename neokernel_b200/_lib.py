@@ -38,7 +38,20 @@ PLAN_MAGIC = 0x4E4B4731
 EXPORTS = ("nk_plan_make", "nk_ws_bytes", "nk_ws_init", "nk_gemm_bf16", "nk_device_error",
            "nk_status_string", "nk_version", "nk_gemm_bf16_static", "nk_gemm_bf16_f32out",
            "nk_rmsnorm_bf16", "nk_qk_norm_rope_cache_bf16", "nk_attention_ws_bytes",
-           "nk_attention_decode_bf16", "nk_silu_mul_bf16")
+           "nk_attention_decode_bf16", "nk_silu_mul_bf16", "nk_peer_buffer_bytes", "nk_peer_alloc",
+           "nk_peer_free", "nk_ipc_handle", "nk_ipc_open", "nk_ipc_close", "nk_allreduce_bf16")
+
+
+NK_PEER_MAX_RANKS = 8
+NK_IPC_HANDLE_BYTES = 64
+NK_PEER_MAX_ELEMS = 1 << 20
+
+
+class NkPeerGroup(ctypes.Structure):
+    """``nk_peer_group`` (include/nk_comm.h)."""
+    _fields_ = [("buf", ctypes.c_void_p * NK_PEER_MAX_RANKS), ("rank", ctypes.c_int32),
+                ("world", ctypes.c_int32), ("max_elems", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
 
 
 class NkPlan(ctypes.Structure):
@@ -114,6 +127,20 @@ def load() -> ctypes.CDLL:
     L.nk_attention_decode_bf16.restype = i32
     L.nk_silu_mul_bf16.argtypes = [vp, vp, i32, i32, vp]
     L.nk_silu_mul_bf16.restype = i32
+    L.nk_peer_buffer_bytes.argtypes = [i32, i32]
+    L.nk_peer_buffer_bytes.restype = ctypes.c_size_t
+    L.nk_peer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
+    L.nk_peer_alloc.restype = i32
+    L.nk_peer_free.argtypes = [vp]
+    L.nk_peer_free.restype = i32
+    L.nk_ipc_handle.argtypes = [vp, vp]
+    L.nk_ipc_handle.restype = i32
+    L.nk_ipc_open.argtypes = [vp, ctypes.POINTER(vp)]
+    L.nk_ipc_open.restype = i32
+    L.nk_ipc_close.argtypes = [vp]
+    L.nk_ipc_close.restype = i32
+    L.nk_allreduce_bf16.argtypes = [vp, vp, i32, ctypes.POINTER(NkPeerGroup), vp]
+    L.nk_allreduce_bf16.restype = i32
     L.nk_device_error.argtypes = [vp, ctypes.POINTER(i32)]
     L.nk_device_error.restype = i32
     L.nk_status_string.argtypes = [i32]

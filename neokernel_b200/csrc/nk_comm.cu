@@ -1,0 +1,176 @@
+// One-shot all-reduce of fp32 partials over NVLink peer memory (include/nk_comm.h).
+//
+// Buffer of one rank (zeroed once, mapped into every rank of the group):
+//   [0, 4 KB)            progress counter of each CTA index (read and advanced by that CTA)
+//   [4 KB, 68 KB)        flags[2 sets][8 source ranks][1024 CTAs], u32
+//   [68 KB, ...)         slots[2 sets][world source ranks][max_elems], fp32
+// Call e (1, 2, ...) of CTA c uses set e & 1: the CTA writes its 1024-element slice of the
+// local partial into slots[set][rank] of every rank, fences at system scope, writes e into
+// flags[set][rank][c] of every rank (release), waits for flags[set][r][c] == e for all r in its
+// own buffer (acquire, bounded) and sums slots[set][0..world) in rank order. Two sets suffice:
+// a rank can only start writing call e+2 into a peer once it has seen that peer's flag for
+// call e+1, i.e. once the peer has finished call e on its stream.
+#include <string.h>
+
+#include "nk_common.cuh"
+#include "../../include/nk_comm.h"
+
+namespace nk {
+
+constexpr int kArThreads = 256;
+constexpr int kArElemsPerCta = kArThreads * 4;
+constexpr int kArMaxCtas = NK_PEER_MAX_ELEMS / kArElemsPerCta;  // 1024
+constexpr size_t kArEpochBytes = (size_t)kArMaxCtas * 4;
+constexpr size_t kArFlagBytes = 2ull * NK_PEER_MAX_RANKS * kArMaxCtas * 4;
+constexpr size_t kArHeader = kArEpochBytes + kArFlagBytes;
+
+struct PeerArgs {
+    uint8_t* buf[NK_PEER_MAX_RANKS];
+    int rank, world, max_elems;
+};
+
+__device__ __forceinline__ unsigned* ar_flag(uint8_t* base, int set, int src, int cta) {
+    return reinterpret_cast<unsigned*>(base + kArEpochBytes) +
+           ((size_t)(set * NK_PEER_MAX_RANKS + src) * kArMaxCtas + cta);
+}
+
+__device__ __forceinline__ float* ar_slot(uint8_t* base, int set, int src, int world,
+                                          int max_elems) {
+    return reinterpret_cast<float*>(base + kArHeader) + (size_t)(set * world + src) * max_elems;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(kArThreads)
+allreduce_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out, int n,
+                      PeerArgs g) {
+    __shared__ unsigned s_e;
+    __shared__ int s_ok;
+    const int c = blockIdx.x;
+    uint8_t* own = g.buf[g.rank];
+    unsigned* epo = reinterpret_cast<unsigned*>(own) + c;
+    if (threadIdx.x == 0) {
+        s_e = *epo + 1u;  // only CTA c of this rank ever touches this counter
+        s_ok = 1;
+    }
+    __syncthreads();
+    const unsigned e = s_e;
+    const int set = (int)(e & 1u);
+    const int i = c * kArElemsPerCta + threadIdx.x * 4;
+    const bool live = i < n;  // n % 4 == 0, so [i, i + 4) is all in or all out
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (live) v = *reinterpret_cast<const float4*>(x + i);
+    // this rank's slice into every rank's buffer (its own included)
+    for (int r = 0; r < g.world; ++r)
+        if (live)
+            *reinterpret_cast<float4*>(ar_slot(g.buf[r], set, g.rank, g.world, g.max_elems) + i) = v;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < g.world) st_release_sys(ar_flag(g.buf[threadIdx.x], set, g.rank, c), e);
+    // every rank's slice of this call in the own buffer
+    if (threadIdx.x < g.world) {
+        const unsigned* f = ar_flag(own, set, threadIdx.x, c);
+        const uint64_t t0 = global_ns();
+        while (ld_acquire_sys(f) != e) {
+            if (global_ns() - t0 > 2000000000ull) {
+                atomicExch(&g_error, NK_ERR_TIMEOUT);
+                s_ok = 0;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    __syncthreads();
+    if (s_ok && live) {
+        float4 a = __ldcg(reinterpret_cast<const float4*>(ar_slot(own, set, 0, g.world, g.max_elems) + i));
+        for (int r = 1; r < g.world; ++r) {
+            const float4 b =
+                __ldcg(reinterpret_cast<const float4*>(ar_slot(own, set, r, g.world, g.max_elems) + i));
+            a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+        }
+        const uint32_t lo = (uint32_t)f32_to_bf16_bits(a.x) | ((uint32_t)f32_to_bf16_bits(a.y) << 16);
+        const uint32_t hi = (uint32_t)f32_to_bf16_bits(a.z) | ((uint32_t)f32_to_bf16_bits(a.w) << 16);
+        *reinterpret_cast<uint2*>(out + i) = make_uint2(lo, hi);
+    }
+    if (threadIdx.x == 0) *epo = e;
+}
+
+}  // namespace nk
+
+using namespace nk;
+
+extern "C" size_t nk_peer_buffer_bytes(int max_elems, int world) {
+    if (max_elems < 1 || max_elems > NK_PEER_MAX_ELEMS || world < 2 || world > NK_PEER_MAX_RANKS)
+        return 0;
+    return kArHeader + 2ull * (size_t)world * (size_t)max_elems * sizeof(float);
+}
+
+extern "C" int nk_peer_alloc(size_t bytes, void** ptr) {
+    if (!ptr || bytes == 0) return NK_ERR_ARG;
+    *ptr = nullptr;
+    if (cudaMalloc(ptr, bytes) != cudaSuccess) return NK_ERR_CUDA;
+    if (cudaMemset(*ptr, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(*ptr);
+        *ptr = nullptr;
+        return NK_ERR_CUDA;
+    }
+    return NK_OK;
+}
+
+extern "C" int nk_peer_free(void* ptr) {
+    if (!ptr) return NK_ERR_ARG;
+    return cudaFree(ptr) == cudaSuccess ? NK_OK : NK_ERR_CUDA;
+}
+
+extern "C" int nk_ipc_handle(void* ptr, void* handle) {
+    static_assert(sizeof(cudaIpcMemHandle_t) == NK_IPC_HANDLE_BYTES, "IPC handle size");
+    if (!ptr || !handle) return NK_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, ptr) != cudaSuccess) return NK_ERR_CUDA;
+    memcpy(handle, &h, sizeof(h));
+    return NK_OK;
+}
+
+extern "C" int nk_ipc_open(const void* handle, void** ptr) {
+    if (!handle || !ptr) return NK_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    *ptr = nullptr;
+    return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess
+               ? NK_OK : NK_ERR_CUDA;
+}
+
+extern "C" int nk_ipc_close(void* ptr) {
+    if (!ptr) return NK_ERR_ARG;
+    return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? NK_OK : NK_ERR_CUDA;
+}
+
+extern "C" int nk_allreduce_bf16(const float* x, void* out, int n, const nk_peer_group* g,
+                                 nk_stream_t stream) {
+    if (!x || !out || !g) return NK_ERR_ARG;
+    if (g->world < 2 || g->world > NK_PEER_MAX_RANKS || g->rank < 0 || g->rank >= g->world ||
+        g->max_elems < 1 || g->max_elems > NK_PEER_MAX_ELEMS)
+        return NK_ERR_ARG;
+    if (n < 1 || n > g->max_elems || n % 4) return NK_ERR_SHAPE;
+    if (((uintptr_t)x & 15u) || ((uintptr_t)out & 15u) || (g->max_elems % 4)) return NK_ERR_ALIGN;
+    PeerArgs a;
+    for (int r = 0; r < NK_PEER_MAX_RANKS; ++r) {
+        a.buf[r] = static_cast<uint8_t*>(r < g->world ? g->buf[r] : nullptr);
+        if (r < g->world && (!a.buf[r] || ((uintptr_t)a.buf[r] & 255u))) return NK_ERR_ARG;
+    }
+    a.rank = g->rank;
+    a.world = g->world;
+    a.max_elems = g->max_elems;
+    const int grid = (n + kArElemsPerCta - 1) / kArElemsPerCta;
+    allreduce_bf16_kernel<<<grid, kArThreads, 0, (cudaStream_t)stream>>>(
+        x, static_cast<__nv_bfloat16*>(out), n, a);
+    return cudaGetLastError() == cudaSuccess ? NK_OK : NK_ERR_CUDA;
+}

@@ -6,3 +6,4 @@
 #include "nk_abi.cu"
 #include "nk_static.cu"
 #include "nk_decode.cu"
+#include "nk_comm.cu"

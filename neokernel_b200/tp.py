@@ -9,8 +9,11 @@ shards the decode linears where their weights shard naturally:
 * gate_up (decode.py:64) is split by output column with the gate and up slices paired, so
   bf16(silu(gate)) * up is local;
 * o_proj (decode.py:58) and down (decode.py:66) are split along K: each rank computes an
-  unrounded fp32 partial (``mm_f32``), the partials are summed with one all-reduce over NCCL
-  (NVLink / NVSwitch), and the sum is rounded to bf16 once — the single-GPU rounding;
+  unrounded fp32 partial (``mm_f32``), the partials are summed across ranks and the sum is
+  rounded to bf16 once — the single-GPU rounding. On GPUs the sum is ``nk_allreduce_bf16``
+  (neokernel_b200/peer.py): one launch per rank that writes its partial into every rank's
+  buffer over NVLink and adds the ranks in rank order; ``collective="nccl"`` uses NCCL's
+  all-reduce instead (and CPU process groups always use ``dist.all_reduce``);
 * lm_head (engine.py:114) is split by vocabulary row: each rank takes its local max and its
   lowest index, and an all-gather of (value, index) picks the global maximum, ties to the
   lowest vocabulary index as torch.argmax does (engine.py:116).
@@ -94,14 +97,23 @@ class TPWeights:
         self.vocab_offset = rank * vl
 
 
-def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None):
+PEER_MAX_AUTO = 1 << 16  # fp32 elements up to which "auto" sums partials over peer memory
+
+
+def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None, collective="auto"):
     """Return ``make(state) -> (row_linear, head)`` for ``qwen3.GraphDecoder`` / ``decode_step``.
 
     ``linear_f32(a, b, out)`` computes an unrounded fp32 partial (default:
     ``neokernel_b200.mm_f32``); ``linear(a, b, out)`` the bf16 lm_head shard (default:
-    ``neokernel_b200.mm``). Buffers are allocated here, once per state, so the hooks are
-    capture-safe.
+    ``neokernel_b200.mm``). ``collective`` sums the partials of the K-split linears: "peer"
+    (``nk_allreduce_bf16`` over NVLink peer memory), "nccl" (``dist.all_reduce``, then the bf16
+    copy) or "auto": peer on a CUDA process group of 2+ ranks for partials of up to
+    ``PEER_MAX_AUTO`` elements, else all_reduce (measured on B200, Qwen3-32B TP=2: the peer
+    sum is ahead at batch 1 and behind NCCL at batch 32). Buffers are allocated here, once per
+    state, so the hooks are capture-safe.
     """
+    if collective not in ("auto", "peer", "nccl"):
+        raise ValueError(f"collective must be auto, peer or nccl, not {collective!r}")
     if linear_f32 is None or linear is None:
         import neokernel_b200 as nk
         linear_f32 = linear_f32 or nk.mm_f32
@@ -111,6 +123,13 @@ def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None):
     def make(st: qwen3.DecodeState):
         B, H = st.batch, w.dims.hidden
         dev = st.x.device
+        use_peer = world > 1 and (collective == "peer" or (
+            collective == "auto" and dev.type == "cuda" and dist.get_backend(group) == "nccl"
+            and B * H <= PEER_MAX_AUTO))
+        peer = None
+        if use_peer:
+            from .peer import PeerGroup
+            peer = PeerGroup(B * H, group=group, device=dev)
         partial = torch.empty(B, H, device=dev, dtype=torch.float32)
         best = torch.empty(B, device=dev, dtype=torch.float32)
         best_idx = torch.empty(B, device=dev, dtype=torch.int64)
@@ -119,6 +138,9 @@ def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None):
 
         def row_linear(a, b, out):
             linear_f32(a, b, out=partial)
+            if peer is not None:
+                peer.allreduce_bf16(partial, out)  # rank-order sum, one rounding to bf16
+                return
             if world > 1:
                 dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=group)
             out.copy_(partial)  # the one rounding to bf16 (nearest-even)

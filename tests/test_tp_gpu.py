@@ -1,5 +1,6 @@
-"""Tensor-parallel decode on 2+ GPUs (NCCL over NVLink), CUDA-graph captured, against the
-single-GPU model of the same seed on every rank. Skipped with fewer than two GPUs."""
+"""Tensor-parallel decode on 2+ GPUs, CUDA-graph captured, against the single-GPU model of the
+same seed on every rank, with the K-split partials summed by the peer-memory all-reduce
+(nk_allreduce_bf16) and by NCCL. Skipped with fewer than two GPUs."""
 
 import multiprocessing as mp
 import os
@@ -20,7 +21,7 @@ def free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, collective):
     try:
         import datetime
         import torch.distributed as dist
@@ -41,7 +42,7 @@ def _worker(rank, world, port, q):
         B, cap = 4, 32
         ref = qwen3.GraphDecoder(full, B, cap, nk.mm, device=dev)
         tpg = qwen3.GraphDecoder(shard, B, cap, nk.mm, device=dev,
-                                 make_hooks=tp.make_hooks(shard))
+                                 make_hooks=tp.make_hooks(shard, collective=collective))
         gen = torch.Generator(device=dev).manual_seed(77)
         worst, agree, total = 0.0, 0, 0
         vl = d.vocab // world
@@ -67,12 +68,14 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(N_GPUS < 2, reason="needs two or more GPUs")
-def test_tp_decode_matches_single_gpu_model():
+@pytest.mark.parametrize("collective", ("peer", "nccl"))
+def test_tp_decode_matches_single_gpu_model(collective):
     world = 4 if N_GPUS >= 4 else 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, collective))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = sorted((q.get(timeout=600) for _ in range(world)), key=lambda r: r[0])
