@@ -110,6 +110,15 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     return p;
 }
 
+// Untiled bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from global
+// into this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -215,7 +224,7 @@ struct TcSmem {
     static constexpr int kStagesFit = (kBudget - 2048) / kStage;
     static constexpr int kStages = kStagesFit > 8 ? 8 : (kStagesFit < 2 ? 2 : kStagesFit);
     static constexpr int kBarOff = kStages * kStage;
-    static constexpr int kNumBars = 2 * kStages + 4;     // full, empty, tfull[2], tempty[2]
+    static constexpr int kNumBars = 2 * kStages + 6;     // full, empty, tfull[2], tempty[2], part[2]
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
     static constexpr int kBytes = kMiscOff + 16;         // tmem slot, abort flag, last flag
     static constexpr int kAlloc = kBytes + 1024;         // slack to align the base to 1 KB
@@ -367,6 +376,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
     const uint32_t bar_empty = bar_full + STAGES * 8;
     const uint32_t bar_tfull = bar_empty + STAGES * 8;
     const uint32_t bar_tempty = bar_tfull + 2 * 8;
+    const uint32_t bar_part = bar_tempty + 2 * 8;
     volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(gbase + L::kMiscOff);
     volatile uint32_t* tmem_slot = misc;
     volatile uint32_t* abort_flag = misc + 1;
@@ -380,6 +390,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar_tfull + 8 * i, 1);
             mbar_init(bar_tempty + 8 * i, kTcEpiThreads / 32);
+            mbar_init(bar_part + 8 * i, 1);
         }
         *abort_flag = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -584,7 +595,60 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                 }
             } else {
                 // own + (rank 1 + rank 2 + ...): a fixed order, whichever rank is late
-                if (ok) {
+                constexpr uint32_t kChunkBytes = 16u * kTcRows * 4u;  // 16 columns of one rank
+                constexpr uint32_t kHalf = (uint32_t)(STAGES * L::kStage) / 2u;
+                const int partners = nseg - 1;
+                const bool bulk = NT != 16 && !tagged && got && partners >= 1 &&
+                                  (uint32_t)partners * kChunkBytes <= kHalf;
+                if (ok && bulk) {
+                    // Every MMA of this CTA is done, so the shared-memory ring is idle: pull each
+                    // partner's partial columns [16k, 16k + 16) — contiguous fp32, [column][128
+                    // rows] — with one bulk copy per rank into alternate halves of the ring, two
+                    // chunks in flight, and add them from shared memory.
+                    const float* tile_part =
+                        a.part + ((size_t)sg.t * a.segments * a.part_cols) * kTcRows;
+                    const int nchunks = (mcount + 15) / 16;
+                    auto issue = [&](int k) {  // one thread
+                        const int h = k & 1;
+                        const int cols = min(16, a.part_cols - 16 * k);  // never past the tile
+                        const uint32_t bytes = (uint32_t)cols * kTcRows * 4u;
+                        mbar_expect_tx(bar_part + 8 * h, (uint32_t)partners * bytes);
+                        for (int i = 0; i < partners; ++i)
+                            bulk_load(base + h * kHalf + (uint32_t)i * kChunkBytes,
+                                      tile_part + ((size_t)(1 + i) * a.part_cols + 16 * k) * kTcRows,
+                                      bytes, bar_part + 8 * h);
+                    };
+                    if (ep == 0) {
+                        issue(0);
+                        if (nchunks > 1) issue(1);
+                    }
+#pragma unroll 1
+                    for (int k = 0; k < nchunks; ++k) {
+                        const int h = k & 1;
+                        const bool arrived =
+                            __all_sync(0xffffffffu, mbar_wait(bar_part + 8 * h, (uint32_t)(k >> 1) & 1u));
+                        float v[16];
+                        tmem_ld16(taddr + 16 * k, v);
+                        const float* sm = reinterpret_cast<const float*>(gbase + h * kHalf) + row;
+                        float ps[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) ps[j] = 0.f;
+                        for (int i = 0; i < partners; ++i)
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) ps[j] += sm[(i * 16 + j) * kTcRows];
+                        if (arrived && n < a.N) {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                if (16 * k + j < mcount)
+                                    store_out(a, (int64_t)(m0 + 16 * k + j) * a.ldy + n, v[j] + ps[j]);
+                        }
+                        epi_bar();  // every thread is done with this half
+                        if (ep == 0 && k + 2 < nchunks) {
+                            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                            issue(k + 2);
+                        }
+                    }
+                } else if (ok) {
 #pragma unroll 1
                     for (int c0 = 0; c0 < NT; c0 += 16) {
                         if (c0 >= mcount) break;  // warp-uniform
