@@ -281,20 +281,21 @@ __device__ __forceinline__ void sum_partials16(const float* part0, int part_cols
 
 // ps[j] += the partials of ranks 1, 2, ..., nseg-1 (in that order) at token columns
 // c0 + j < mcount of one tile row (slot0: the row's rank-0, column-0 slot), clearing each
-// slot it reads. Slots are read four ranks x four columns at a time; while some are not yet
+// slot it reads. Slots are read RB ranks x CB columns at a time; while some are not yet
 // published, all of those are read again together (one L2 round trip per round), bounded by
 // ~2 s (then NK_ERR_TIMEOUT is recorded and false returned).
-__device__ __forceinline__ bool collect_partials16(uint64_t* slot0, int part_cols, int c0,
-                                                   int nseg, int mcount, float (&ps)[16]) {
-    for (int r0 = 1; r0 < nseg; r0 += 4) {
+template <int RB, int CB>
+__device__ __forceinline__ bool collect_rounds(uint64_t* slot0, int part_cols, int c0, int nseg,
+                                               int mcount, float (&ps)[16]) {
+    for (int r0 = 1; r0 < nseg; r0 += RB) {
 #pragma unroll
-        for (int j0 = 0; j0 < 16; j0 += 4) {
+        for (int j0 = 0; j0 < 16; j0 += CB) {
             if (c0 + j0 >= mcount) break;
-            uint64_t x[4][4];
+            uint64_t x[RB][CB];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < RB; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
+                for (int j = 0; j < CB; ++j)
                     x[i][j] = (r0 + i < nseg && c0 + j0 + j < mcount)
                                   ? ld_slot(slot0 + ((size_t)(r0 + i) * part_cols + c0 + j0 + j) * kTcRows)
                                   : ((uint64_t)kSlotTag << 32);
@@ -302,9 +303,9 @@ __device__ __forceinline__ bool collect_partials16(uint64_t* slot0, int part_col
             for (;;) {
                 bool all = true;
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
+                for (int i = 0; i < RB; ++i)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) all &= (uint32_t)(x[i][j] >> 32) == kSlotTag;
+                    for (int j = 0; j < CB; ++j) all &= (uint32_t)(x[i][j] >> 32) == kSlotTag;
                 if (all) break;
                 if (t0 == 0) t0 = global_ns();
                 if (global_ns() - t0 > 2000000000ull) {
@@ -313,16 +314,16 @@ __device__ __forceinline__ bool collect_partials16(uint64_t* slot0, int part_col
                 }
                 __nanosleep(32);
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
+                for (int i = 0; i < RB; ++i)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
+                    for (int j = 0; j < CB; ++j)
                         if ((uint32_t)(x[i][j] >> 32) != kSlotTag)
                             x[i][j] = ld_slot(slot0 + ((size_t)(r0 + i) * part_cols + c0 + j0 + j) * kTcRows);
             }
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < RB; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
+                for (int j = 0; j < CB; ++j)
                     if (r0 + i < nseg && c0 + j0 + j < mcount) {
                         ps[j0 + j] += __uint_as_float((uint32_t)x[i][j]);
                         clear_slot(slot0 + ((size_t)(r0 + i) * part_cols + c0 + j0 + j) * kTcRows);
@@ -330,6 +331,16 @@ __device__ __forceinline__ bool collect_partials16(uint64_t* slot0, int part_col
         }
     }
     return true;
+}
+
+// The round shape follows the chunk's width: one token column reads up to 16 ranks per round
+// (a small tile is shared by 5-7 CTAs), wider chunks four ranks by four columns.
+__device__ __forceinline__ bool collect_partials16(uint64_t* slot0, int part_cols, int c0,
+                                                   int nseg, int mcount, float (&ps)[16]) {
+    const int w = mcount - c0;
+    if (w <= 1) return collect_rounds<16, 1>(slot0, part_cols, c0, nseg, mcount, ps);
+    if (w <= 2) return collect_rounds<8, 2>(slot0, part_cols, c0, nseg, mcount, ps);
+    return collect_rounds<4, 4>(slot0, part_cols, c0, nseg, mcount, ps);
 }
 
 // One tile segment of this CTA's unit range.
@@ -655,7 +666,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                         if constexpr (NT != 16) {
 #pragma unroll
                             for (int j = 0; j < 16; ++j) psum[j] = 0.f;
-                            if (tagged) got = collect_partials16(slot0, a.part_cols, c0, nseg, mcount, psum);
+                            if (tagged) got = collect_rounds<4, 4>(slot0, a.part_cols, c0, nseg, mcount, psum);
                             else if (got) sum_partials16(part0, a.part_cols, c0, nseg, mcount, psum);
                             __syncwarp();  // converge before tcgen05.ld
                         }
