@@ -695,13 +695,13 @@ def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, war
     this run: QKV/gate_up split by column, o_proj/down by K with their fp32 partials summed
     across ranks, lm_head by vocabulary; one CUDA graph per batch; KV length 2048. The
     product ("auto") sums the partials with the peer-memory all-reduce (nk_allreduce_bf16) for
-    small batches and NCCL's all-reduce for large ones; at N > 1 the step with each of the two
-    throughout is timed beside it. tok/s counts each sequence's token once (the ranks share
-    one model)."""
+    small batches and NCCL's all-reduce for large ones; at N > 1 the step with NCCL's
+    all-reduce throughout is timed beside it. tok/s counts each sequence's token once (the
+    ranks share one model)."""
     from neokernel_b200 import qwen3, tp
     d = qwen3.QWEN3_32B
     w = tp.TPWeights(d, seed=13, rank=rank, world=world, device=dev)
-    arms = ("auto", "peer", "nccl") if world > 1 else ("auto",)
+    arms = ("auto", "nccl") if world > 1 else ("auto",)
     out = {}
     for collective in arms:
         res = {}
@@ -735,7 +735,7 @@ def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, war
     torch.cuda.empty_cache()
     return {"model": "qwen3-32b random-init, 64 layers, hidden 5120, MLP 25600, 64Q/8KV x 128",
             "tp": world, "kv_length": kv, "steps": steps, "batches": out["auto"],
-            "batches_peer_allreduce": out.get("peer"), "batches_nccl_allreduce": out.get("nccl"),
+            "batches_nccl_allreduce": out.get("nccl"),
             "collectives": "fp32 partials of o_proj and down summed across ranks, one bf16 "
                            "rounding: nk_allreduce_bf16 over NVLink peer memory (rank order) up "
                            "to 64K elements, NCCL all-reduce above; NCCL all-gather of (max, "
