@@ -99,10 +99,11 @@ typedef struct nk_plan {
 NK_API int nk_plan_make(nk_plan* plan, int M_max, int N, int K, int split_k, int kind);
 
 /* Bytes of device workspace nk_gemm_bf16 needs for this plan: a fixed 256 KiB region of
- * split-K tickets followed by the fp32 partials. 0 when the plan needs none (split_k == 1).
+ * split-K tickets followed by the partial sums (8 bytes per partial value for the
+ * tensor-core family, 4 for the GEMV family). 0 when the plan needs none (no tile is split).
  * One workspace (zeroed once by nk_ws_init) can serve any sequence of ordered calls whatever
  * their plans, if it is as large as the largest plan needs: every plan uses the same ticket
- * region and the kernels leave it zeroed. Plans with split_k > 1 and more than 65536 output
+ * region and the kernels leave the tickets and the partial slots they read zeroed. Plans with split_k > 1 and more than 65536 output
  * tiles are refused (NK_ERR_SPLIT). */
 NK_API size_t nk_ws_bytes(const nk_plan* plan);
 
@@ -142,8 +143,8 @@ NK_API int nk_gemm_bf16(const void* x, int64_t ldx,
  * NK_ERR_WORKSPACE. Nothing is allocated. The first call on each device (with that device
  * current) looks up the array's device address, so make it before any stream capture on that
  * device. All calls on a device share the array and it keeps the last call's contents: each
- * call clears the tickets it uses, and calls that overlap on the GPU race — order them (one
- * stream, or streams joined by events).
+ * call clears the region it uses first, and calls that overlap on the GPU race — order them
+ * (one stream, or streams joined by events).
  */
 #define NK_STATIC_SCRATCH_BYTES (8u << 20)
 NK_API int nk_gemm_bf16_static(const void* x, int64_t ldx,

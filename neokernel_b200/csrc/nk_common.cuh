@@ -141,10 +141,12 @@ __device__ __forceinline__ void splitk_reduce_tile(const GemmArgsT& a, int n_bas
     }
 }
 
-// Workspace layout: a fixed region of kTicketsMax split-K tickets at offset 0, then the fp32
-// partials [split][M_max][N]. Every plan puts its tickets in the same fixed region and the
-// kernels always leave them at zero, so any sequence of ordered calls may share one
-// workspace whatever their plans (one plan's partials never overlay another's tickets).
+// Workspace layout: a fixed region of kTicketsMax split-K tickets at offset 0, then the
+// partials — [split][M_max][N] fp32 for the GEMV family, [tile][segment][token column][128
+// rows] 64-bit slots for the tensor-core family. Every plan puts its tickets in the same fixed
+// region, the kernels leave the tickets at zero and clear every tagged slot they read, so any
+// sequence of ordered calls may share one workspace whatever their plans (one plan's
+// partials never overlay another's tickets).
 constexpr size_t kTicketsMax = 65536;
 constexpr size_t kTicketBytes = kTicketsMax * sizeof(unsigned);
 

@@ -19,8 +19,9 @@
 //                   each tile segment tcgen05.commit -> tfull[buf].
 //   warps 2..5    : epilogue. Warp w reads TMEM lanes 32*(w%4).. (row n of the tile) with
 //                   tcgen05.ld, frees the accumulator (tempty[buf]) and stores bf16 y when the
-//                   segment covers the whole K range; otherwise it stores an fp32 partial and
-//                   the CTA that completes the tile (ticket) sums its partials in rank order.
+//                   segment covers the whole K range. A tile shared by several CTAs is
+//                   finished by its rank-0 CTA (the one holding its first K blocks) from the
+//                   other ranks' fp32 partials, added in rank order (protocols below).
 // The two accumulators let the epilogue of one segment overlap the MMAs of the next.
 //
 // Programmatic dependent launch: weights do not depend on the previous kernel, so the
