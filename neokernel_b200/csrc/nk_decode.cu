@@ -171,21 +171,17 @@ qk_norm_rope_cache_kernel(const __nv_bfloat16* qkv, int64_t ld_qkv, const __nv_b
 // are in flight: every thread first issues its share of the chunk's K rows, then of its V
 // rows, as asynchronous copies into shared memory (16 or 8 bytes each; rows past the
 // position are zero-filled without a read), so the whole 2 x 16 KB chunk is requested at
-// once. Warp w then scores rows [16w, 16w + 16) in two batches of 8: lane l forms the
-// partial dot products of elements 4l..4l+3, a recursive-halving reduction leaves each
-// (row, head) score on its owner lanes, which alone evaluate the exponentials of the
-// online softmax and pass the batch's probabilities to the whole warp through shared
-// memory for the V accumulation (lane l again holding elements 4l..4l+3). The warps' states are combined in shared memory
-// and the CTA stores (max, sum, unnormalised acc); a merge kernel combines the splits:
+// once. The two contractions then run on the tensor cores (mma.sync m16n8k16, the query
+// heads as rows of a 16-row tile), with an fp32 softmax in between (details at the kernel).
+// The warps' states are combined in shared memory and the CTA stores (max, sum,
+// unnormalised acc); a merge kernel combines the splits:
 // out = sum_s e^(m_s-M) acc_s / sum_s e^(m_s-M) l_s. CTAs whose chunk starts past the
 // position store nothing (the merge reads only the splits at or below it).
 // ---------------------------------------------------------------------------------------
 constexpr int kAttnChunk = 64;
 constexpr int kAttnThreads = 128;
 constexpr int kAttnMaxGroup = 8;
-constexpr int kAttnBatch = 8;                       // rows scored together by a warp
 constexpr int kAttnRowBytes = kHeadDim * 2;         // 256 B per cache row
-constexpr int kAttnTileBytes = kAttnChunk * kAttnRowBytes;  // 16 KB per K or V chunk
 
 template <int VB>
 __device__ __forceinline__ void cp_async(uint32_t dst, const void* src, bool valid) {
@@ -198,76 +194,67 @@ __device__ __forceinline__ void cp_async(uint32_t dst, const void* src, bool val
                      : "memory");
 }
 
-// Copies rows [0, C) of one cache chunk into a [C][128] bf16 tile; rows >= valid are zeros.
+// K and V rows sit 16 bytes apart more than their 256 bytes in shared memory, so that the
+// fragment loads of 8 consecutive rows hit 8 different bank groups.
+constexpr int kAttnPitch = kAttnRowBytes + 16;
+constexpr int kAttnPTile = kAttnChunk * kAttnPitch;
+
 template <int VB>
 __device__ __forceinline__ void attn_load_tile(uint32_t tile, const __nv_bfloat16* rows0,
                                                int64_t cs, int valid) {
-    constexpr int kSegs = kAttnRowBytes / VB;  // copies per row
+    constexpr int kSegs = kAttnRowBytes / VB;
 #pragma unroll
     for (int i = 0; i < kAttnChunk * kSegs / kAttnThreads; ++i) {
         const int idx = i * kAttnThreads + threadIdx.x;
         const int row = idx / kSegs, seg = idx - row * kSegs;
         const bool ok = row < valid;
         const __nv_bfloat16* src = rows0 + (int64_t)(ok ? row : 0) * cs + seg * (VB / 2);
-        cp_async<VB>(tile + row * kAttnRowBytes + seg * VB, src, ok);
+        cp_async<VB>(tile + row * kAttnPitch + seg * VB, src, ok);
     }
 }
 
-// Sums the 8 x G scores of a batch (value i = r * G + g, one partial per lane) across the
-// warp by recursive halving: at offset o a lane keeps the half of its values selected by
-// bit o of its lane id and adds the partner's copy of that half, so 8G values need 8G - 1
-// shuffles instead of 5 * 8G. Afterwards lane l holds the full sums of rows r = l >> 2 and
-// heads g = own_head(l, j), j < kOwned (duplicated over the low lane bits when G < 4).
-template <int G>
-struct AttnOwn {
-    static constexpr int kValues = kAttnBatch * G;
-    static constexpr int kOwned = G == 8 ? 2 : 1;
-    static constexpr int kLog2G = G == 8 ? 3 : G == 4 ? 2 : G == 2 ? 1 : 0;
-    __device__ static __forceinline__ int head(int lane, int j) {
-        return G == 8 ? 2 * (lane & 3) + j : (lane >> (2 - kLog2G)) & (G - 1);
-    }
-};
-
-template <int G>
-__device__ __forceinline__ void attn_reduce_scores(float (&v)[kAttnBatch * G], int lane) {
-    constexpr int NV = kAttnBatch * G;
-#pragma unroll
-    for (int k = 0; k < 5; ++k) {
-        const int o = 16 >> k;
-        const int n = NV >> k;  // values still held before this step (constant once unrolled)
-        if (n > AttnOwn<G>::kOwned) {
-            const bool up = (lane & o) != 0;
-#pragma unroll
-            for (int j = 0; j < n / 2; ++j) {
-                const float send = up ? v[j] : v[j + n / 2];
-                const float keep = up ? v[j + n / 2] : v[j];
-                v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < AttnOwn<G>::kOwned; ++j) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
-        }
-    }
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                          uint32_t b1) {
+    // rows 8..15 of A are zero (at most 8 query heads per KV head)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                              uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    return (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+}
+
+// CTA (split, kv head, sequence); warp w owns cache rows [16w, 16w + 16) of the chunk.
+// Lane (g = lane / 4, t = lane % 4) follows the m16n8k16 fragment layout: query head g
+// (rows g >= G are zero), keys 2t, 2t+1, 8+2t, 9+2t of the warp's 16. S = Q K^T (two 8-key
+// tiles, eight 16-dim steps) accumulates exact bf16 products in fp32; the softmax is fp32;
+// P V uses P = P_hi + P_lo (two bf16 halves, so P keeps ~16 bits) against bf16 V,
+// accumulated in fp32 over 16 tiles of 8 dimensions.
 template <int G, int VB>
 __global__ void __launch_bounds__(kAttnThreads)
 attn_partial_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
                     const __nv_bfloat16* v_cache, const int64_t* position, float* part_acc,
                     float* part_ml, int Hq, int Hkv, int splits, int capacity, int64_t cb,
                     int64_t ch, int64_t cs, float scale) {
-    using O = AttnOwn<G>;
-    constexpr int NO = O::kOwned;
-    // K tile, V tile; after scoring, the K tile holds the warps' accumulators
-    __shared__ __align__(128) uint8_t s_tiles[2 * kAttnTileBytes];
-    __shared__ __align__(16) float s_p[4][kAttnBatch][G];  // a warp's batch probabilities
-    __shared__ __align__(16) float s_c[4][G];              // ... and running-sum rescales
+    __shared__ __align__(128) uint8_t s_tiles[2 * kAttnPTile];
     __shared__ float s_m[4][G], s_l[4][G];
-    static_assert(4 * G * kHeadDim * 4 <= kAttnTileBytes, "accumulators must fit the K tile");
+    static_assert(G <= 8, "at most 8 query heads per KV head");
+    static_assert(4 * G * kHeadDim * 4 <= kAttnPTile, "accumulators must fit the K tile");
     if (threadIdx.x == 0) griddep_launch_dependents();
     griddep_wait();
     const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
     const int64_t pos_in = *position;
     const int64_t pos = min(pos_in, (int64_t)capacity - 1);  // never past the cache
     if ((pos_in < 0 || pos_in >= capacity) && split == 0 && kh == 0 && b == 0 && threadIdx.x == 0)
@@ -276,125 +263,109 @@ attn_partial_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
     if ((int64_t)j0 > pos) return;  // also every CTA when the position is negative
     const int valid = (int)min((int64_t)kAttnChunk, pos + 1 - j0);
 
-    const uint32_t sk = smem_u32(s_tiles), sv = sk + kAttnTileBytes;
+    const uint32_t sk = smem_u32(s_tiles), sv = sk + kAttnPTile;
     const int64_t base = (int64_t)b * cb + (int64_t)kh * ch + (int64_t)j0 * cs;
     attn_load_tile<VB>(sk, k_cache + base, cs, valid);
     asm volatile("cp.async.commit_group;" ::: "memory");
     attn_load_tile<VB>(sv, v_cache + base, cs, valid);
     asm volatile("cp.async.commit_group;" ::: "memory");
 
-    float qf[G][4];
+    // A fragments of Q: head g, dimensions 16ks + 2t (+1) and 16ks + 8 + 2t (+1)
+    uint32_t qa[8][2];
+    {
+        const __nv_bfloat16* qr = q + ((int64_t)b * Hq + kh * G + (g < G ? g : 0)) * kHeadDim;
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const __nv_bfloat16* qp = q + ((int64_t)b * Hq + kh * G + g) * kHeadDim + lane * 4;
-        const uint2 qv = *reinterpret_cast<const uint2*>(qp);
-        qf[g][0] = bf16lo(qv.x); qf[g][1] = bf16hi(qv.x);
-        qf[g][2] = bf16lo(qv.y); qf[g][3] = bf16hi(qv.y);
+        for (int ks = 0; ks < 8; ++ks) {
+            qa[ks][0] = g < G ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 2 * t) : 0u;
+            qa[ks][1] = g < G ? *reinterpret_cast<const uint32_t*>(qr + 16 * ks + 8 + 2 * t) : 0u;
+        }
     }
-    float acc[G][4];
-#pragma unroll
-    for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
-    float m_own[NO], l_own[NO];  // running max and sum of the heads this lane owns
-#pragma unroll
-    for (int j = 0; j < NO; ++j) { m_own[j] = -INFINITY; l_own[j] = 0.f; }
-    const int r_own = lane >> 2;
-    const uint8_t* kt = s_tiles + lane * 8;
-    const uint8_t* vt = s_tiles + kAttnTileBytes + lane * 8;
 
     asm volatile("cp.async.wait_group 1;" ::: "memory");  // this thread's K copies landed
     __syncthreads();                                     // ... and everyone's
+    float sc[2][4];
 #pragma unroll
-    for (int bt = 0; bt < 2; ++bt) {
-        const int r0 = warp * 16 + bt * kAttnBatch;
-        float sc[O::kValues];
+    for (int nt = 0; nt < 2; ++nt) {
+        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+        const uint8_t* kr = s_tiles + (warp * 16 + nt * 8 + g) * kAttnPitch + 4 * t;
 #pragma unroll
-        for (int r = 0; r < kAttnBatch; ++r) {
-            const uint2 kv = *reinterpret_cast<const uint2*>(kt + (r0 + r) * kAttnRowBytes);
-            const float k0 = bf16lo(kv.x), k1 = bf16hi(kv.x), k2 = bf16lo(kv.y), k3 = bf16hi(kv.y);
-#pragma unroll
-            for (int g = 0; g < G; ++g)
-                sc[r * G + g] = qf[g][0] * k0 + qf[g][1] * k1 + qf[g][2] * k2 + qf[g][3] * k3;
+        for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + 32 * ks);
+            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + 32 * ks + 16);
+            mma_16816(sc[nt], qa[ks][0], qa[ks][1], b0, b1);
         }
-        attn_reduce_scores<G>(sc, lane);
-        const bool row_ok = r0 + r_own < valid;
-#pragma unroll
-        for (int j = 0; j < NO; ++j) {
-            const float x = row_ok ? sc[j] * scale : -INFINITY;
-            float bm = x;  // batch max over the 8 rows (lane bits 2-4) of this head
-            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
-            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
-            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
-            const float mn = fmaxf(m_own[j], bm);
-            const bool any = mn != -INFINITY;
-            const float corr = any ? expf(m_own[j] - mn) : 1.f;  // 0 while m is still -inf
-            const float p = any ? expf(x - mn) : 0.f;            // 0 for rows past the position
-            float ps = p;
-            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-            ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-            ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-            l_own[j] = l_own[j] * corr + ps;
-            m_own[j] = mn;
-            const int g = O::head(lane, j);
-            s_p[warp][r_own][g] = p;
-            if (r_own == 0) s_c[warp][g] = corr;
-        }
-        if (bt == 0) {
-            asm volatile("cp.async.wait_group 0;" ::: "memory");  // V copies landed
-            __syncthreads();
-        } else {
-            __syncwarp();
-        }
-        float vr[kAttnBatch][4];
-#pragma unroll
-        for (int r = 0; r < kAttnBatch; ++r) {
-            const uint2 vv = *reinterpret_cast<const uint2*>(vt + (r0 + r) * kAttnRowBytes);
-            vr[r][0] = bf16lo(vv.x); vr[r][1] = bf16hi(vv.x);
-            vr[r][2] = bf16lo(vv.y); vr[r][3] = bf16hi(vv.y);
-        }
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const float c = s_c[warp][g];
-            float a0 = acc[g][0] * c, a1 = acc[g][1] * c, a2 = acc[g][2] * c, a3 = acc[g][3] * c;
-#pragma unroll
-            for (int r = 0; r < kAttnBatch; ++r) {
-                const float p = s_p[warp][r][g];
-                a0 += p * vr[r][0]; a1 += p * vr[r][1]; a2 += p * vr[r][2]; a3 += p * vr[r][3];
-            }
-            acc[g][0] = a0; acc[g][1] = a1; acc[g][2] = a2; acc[g][3] = a3;
-        }
-        __syncwarp();  // the next batch overwrites s_p and s_c
     }
-    if (r_own == 0) {
+    // this lane's scores of head g: keys r0 + 2t, r0 + 2t + 1, r0 + 8 + 2t, r0 + 9 + 2t
+    const int r0 = warp * 16;
+    float x[4] = {sc[0][0], sc[0][1], sc[1][0], sc[1][1]};
+    const int kk[4] = {r0 + 2 * t, r0 + 2 * t + 1, r0 + 8 + 2 * t, r0 + 9 + 2 * t};
+    float m = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < NO; ++j) {
-            const int g = O::head(lane, j);
-            s_m[warp][g] = m_own[j];
-            s_l[warp][g] = l_own[j];
-        }
+    for (int i = 0; i < 4; ++i) {
+        x[i] = kk[i] < valid ? x[i] * scale : -INFINITY;
+        m = fmaxf(m, x[i]);
+    }
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    float p[4], l = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        p[i] = m == -INFINITY ? 0.f : expf(x[i] - m);  // 0 for rows past the position
+        l += p[i];
+    }
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    // P as A fragments, split into a bf16 high part and the bf16 rounding of the rest
+    const uint32_t ph0 = pack_bf16x2(p[0], p[1]), ph2 = pack_bf16x2(p[2], p[3]);
+    const uint32_t pl0 = pack_bf16x2(p[0] - bf16lo(ph0), p[1] - bf16hi(ph0));
+    const uint32_t pl2 = pack_bf16x2(p[2] - bf16lo(ph2), p[3] - bf16hi(ph2));
+
+    asm volatile("cp.async.wait_group 0;" ::: "memory");  // V copies landed
+    __syncthreads();
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    // ldmatrix.trans row addresses: matrix mi = lane / 8 = (keys half mi & 1, dims +8 (mi >> 1))
+    const int mi = lane >> 3, mr = lane & 7;
+    const uint32_t vrow = sv + (uint32_t)(r0 + (mi & 1) * 8 + mr) * kAttnPitch + (mi >> 1) * 16;
+#pragma unroll
+    for (int n = 0; n < 16; n += 2) {
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4_trans(vrow + n * 16, b00, b01, b10, b11);
+        mma_16816(o[n], ph0, ph2, b00, b01);
+        mma_16816(o[n], pl0, pl2, b00, b01);
+        mma_16816(o[n + 1], ph0, ph2, b10, b11);
+        mma_16816(o[n + 1], pl0, pl2, b10, b11);
     }
     __syncthreads();  // every warp is done with the K tile
     float* s_acc = reinterpret_cast<float*>(s_tiles);  // [4][G][128]
+    if (g < G) {
 #pragma unroll
-    for (int g = 0; g < G; ++g)
-        *reinterpret_cast<float4*>(s_acc + (warp * G + g) * kHeadDim + lane * 4) =
-            make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+        for (int n = 0; n < 16; ++n)
+            *reinterpret_cast<float2*>(s_acc + (warp * G + g) * kHeadDim + 8 * n + 2 * t) =
+                make_float2(o[n][0], o[n][1]);
+        if (t == 0) {
+            s_m[warp][g] = m;
+            s_l[warp][g] = l;
+        }
+    }
     __syncthreads();
     // thread t combines element d = t of every query head of the group
     const int d = threadIdx.x;
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
+    for (int gg = 0; gg < G; ++gg) {
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w][g]);
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w][gg]);
         float L = 0.f, A = 0.f;
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
-            if (s_m[w][g] == -INFINITY) continue;  // a warp whose rows are all past the position
-            const float f = expf(s_m[w][g] - M);
-            L += s_l[w][g] * f;
-            A += s_acc[(w * G + g) * kHeadDim + d] * f;
+            if (s_m[w][gg] == -INFINITY) continue;  // a warp whose rows are all past the position
+            const float f = expf(s_m[w][gg] - M);
+            L += s_l[w][gg] * f;
+            A += s_acc[(w * G + gg) * kHeadDim + d] * f;
         }
-        const int64_t hrow = ((int64_t)b * Hq + kh * G + g) * splits + split;
+        const int64_t hrow = ((int64_t)b * Hq + kh * G + gg) * splits + split;
         part_acc[hrow * kHeadDim + d] = A;
         if (d == 0) {
             part_ml[hrow * 2] = M;
@@ -548,10 +519,9 @@ extern "C" int nk_attention_decode_bf16(const void* q, const void* k_cache, cons
                       cache_head_stride % 8 == 0 && cache_batch_stride % 8 == 0;
     int st;
 #define NK_ATTN_LAUNCH(GG, VB)                                                                  \
-    launch_pdl_smem(attn_partial_kernel<GG, VB>, grid, dim3(kAttnThreads), 0, s, qq, kk, vv,   \
+    launch_pdl_smem(attn_partial_kernel<GG, VB>, grid, dim3(kAttnThreads), 0, s, qq, kk, vv,    \
                     position, part_acc, part_ml, q_heads, kv_heads, splits, capacity,           \
-                    cache_batch_stride,                                                       \
-                    cache_head_stride, cache_seq_stride, scale)
+                    cache_batch_stride, cache_head_stride, cache_seq_stride, scale)
     switch (G) {
         case 1: st = wide ? NK_ATTN_LAUNCH(1, 16) : NK_ATTN_LAUNCH(1, 8); break;
         case 2: st = wide ? NK_ATTN_LAUNCH(2, 16) : NK_ATTN_LAUNCH(2, 8); break;
