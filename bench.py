@@ -643,8 +643,21 @@ def attention_only(args):
     for _ in range(args.reps):
         ops.attention_decode(q, kc, vc, position, out, ws, H, Hkv)
     torch.cuda.synchronize(dev)
+    # partial + merge timed with CUDA events, L2 flushed (a 256 MB write) before each launch
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(20)]
+    for e0, e1 in ev:
+        flush.zero_()
+        e0.record()
+        ops.attention_decode(q, kc, vc, position, out, ws, H, Hkv)
+        e1.record()
+    torch.cuda.synchronize(dev)
+    us = sorted(e0.elapsed_time(e1) * 1e3 for e0, e1 in ev)
     kv_bytes = 2 * B * Hkv * (kv + 1) * D * 2
-    print(json.dumps({"attention": [B, kv], "reps": args.reps, "kv_bytes": kv_bytes}))
+    print(json.dumps({"attention": [B, kv], "reps": args.reps, "kv_bytes": kv_bytes,
+                      "us_median_cold_l2": round(us[len(us) // 2], 2),
+                      "tbs_cold_l2": round(kv_bytes / (us[len(us) // 2] * 1e-6) / 1e12, 3)}))
     return 0
 
 

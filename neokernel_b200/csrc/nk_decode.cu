@@ -234,22 +234,29 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
 }
 
-// CTA (split, kv head, sequence); warp w owns cache rows [16w, 16w + 16) of the chunk.
+// Two pipeline stages, each one chunk's K tile and V tile.
+constexpr int kAttnStages = 2;
+constexpr int kAttnSmem = kAttnStages * 2 * kAttnPTile;  // 68 KB: 3 CTAs per SM
+
+// CTA (split, kv head, sequence) walks the chunks [c0, c1) of its split (the chunks that
+// hold positions 0..pos, divided evenly over the splits), the copies of chunk c+1 in
+// flight while chunk c is computed. Warp w owns rows [16w, 16w + 16) of every chunk and
+// keeps an online softmax over them (running max m, sum l, unnormalised o).
 // Lane (g = lane / 4, t = lane % 4) follows the m16n8k16 fragment layout: query head g
 // (rows g >= G are zero), keys 2t, 2t+1, 8+2t, 9+2t of the warp's 16. S = Q K^T (two 8-key
 // tiles, eight 16-dim steps) accumulates exact bf16 products in fp32; the softmax is fp32;
 // P V uses P = P_hi + P_lo (two bf16 halves, so P keeps ~16 bits) against bf16 V,
 // accumulated in fp32 over 16 tiles of 8 dimensions.
 template <int G, int VB>
-__global__ void __launch_bounds__(kAttnThreads)
+__global__ void __launch_bounds__(kAttnThreads, 3)
 attn_partial_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
                     const __nv_bfloat16* v_cache, const int64_t* position, float* part_acc,
                     float* part_ml, int Hq, int Hkv, int splits, int capacity, int64_t cb,
                     int64_t ch, int64_t cs, float scale) {
-    __shared__ __align__(128) uint8_t s_tiles[2 * kAttnPTile];
+    extern __shared__ __align__(128) uint8_t s_tiles[];  // [stage][K, V][kAttnPTile]
     __shared__ float s_m[4][G], s_l[4][G];
     static_assert(G <= 8, "at most 8 query heads per KV head");
-    static_assert(4 * G * kHeadDim * 4 <= kAttnPTile, "accumulators must fit the K tile");
+    static_assert(4 * G * kHeadDim * 4 <= kAttnSmem, "accumulators must fit the tiles");
     if (threadIdx.x == 0) griddep_launch_dependents();
     griddep_wait();
     const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
@@ -259,16 +266,33 @@ attn_partial_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
     const int64_t pos = min(pos_in, (int64_t)capacity - 1);  // never past the cache
     if ((pos_in < 0 || pos_in >= capacity) && split == 0 && kh == 0 && b == 0 && threadIdx.x == 0)
         atomicExch(&g_error, NK_ERR_RANGE);
-    const int j0 = split * kAttnChunk;
-    if ((int64_t)j0 > pos) return;  // also every CTA when the position is negative
-    const int valid = (int)min((int64_t)kAttnChunk, pos + 1 - j0);
+    if (pos < 0) return;
+    // chunks [c0, c1) of the n that hold positions 0..pos; with fewer chunks than splits,
+    // split s < n takes chunk s and the others store nothing (the merge reads min(n, splits))
+    const int n = (int)(pos / kAttnChunk) + 1;
+    int c0, c1;
+    if (n >= splits) {
+        c0 = (int)((int64_t)split * n / splits);
+        c1 = (int)((int64_t)(split + 1) * n / splits);
+    } else {
+        if (split >= n) return;
+        c0 = split;
+        c1 = split + 1;
+    }
 
-    const uint32_t sk = smem_u32(s_tiles), sv = sk + kAttnPTile;
-    const int64_t base = (int64_t)b * cb + (int64_t)kh * ch + (int64_t)j0 * cs;
-    attn_load_tile<VB>(sk, k_cache + base, cs, valid);
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    attn_load_tile<VB>(sv, v_cache + base, cs, valid);
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    const uint32_t s0 = smem_u32(s_tiles);
+    const int64_t base = (int64_t)b * cb + (int64_t)kh * ch;
+    auto issue = [&](int c, int stage) {  // K then V of chunk c, one commit group each
+        const int j0 = c * kAttnChunk;
+        const int valid = (int)min((int64_t)kAttnChunk, pos + 1 - j0);
+        const uint32_t sk = s0 + stage * 2 * kAttnPTile;
+        attn_load_tile<VB>(sk, k_cache + base + (int64_t)j0 * cs, cs, valid);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        attn_load_tile<VB>(sk + kAttnPTile, v_cache + base + (int64_t)j0 * cs, cs, valid);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    issue(c0, 0);
+    if (c0 + 1 < c1) issue(c0 + 1, 1);
 
     // A fragments of Q: head g, dimensions 16ks + 2t (+1) and 16ks + 8 + 2t (+1)
     uint32_t qa[8][2];
@@ -281,76 +305,98 @@ attn_partial_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
         }
     }
 
-    asm volatile("cp.async.wait_group 1;" ::: "memory");  // this thread's K copies landed
-    __syncthreads();                                     // ... and everyone's
-    float sc[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-        const uint8_t* kr = s_tiles + (warp * 16 + nt * 8 + g) * kAttnPitch + 4 * t;
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + 32 * ks);
-            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + 32 * ks + 16);
-            mma_16816(sc[nt], qa[ks][0], qa[ks][1], b0, b1);
-        }
-    }
-    // this lane's scores of head g: keys r0 + 2t, r0 + 2t + 1, r0 + 8 + 2t, r0 + 9 + 2t
-    const int r0 = warp * 16;
-    float x[4] = {sc[0][0], sc[0][1], sc[1][0], sc[1][1]};
-    const int kk[4] = {r0 + 2 * t, r0 + 2 * t + 1, r0 + 8 + 2 * t, r0 + 9 + 2 * t};
-    float m = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        x[i] = kk[i] < valid ? x[i] * scale : -INFINITY;
-        m = fmaxf(m, x[i]);
-    }
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    float p[4], l = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        p[i] = m == -INFINITY ? 0.f : expf(x[i] - m);  // 0 for rows past the position
-        l += p[i];
-    }
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    // P as A fragments, split into a bf16 high part and the bf16 rounding of the rest
-    const uint32_t ph0 = pack_bf16x2(p[0], p[1]), ph2 = pack_bf16x2(p[2], p[3]);
-    const uint32_t pl0 = pack_bf16x2(p[0] - bf16lo(ph0), p[1] - bf16hi(ph0));
-    const uint32_t pl2 = pack_bf16x2(p[2] - bf16lo(ph2), p[3] - bf16hi(ph2));
-
-    asm volatile("cp.async.wait_group 0;" ::: "memory");  // V copies landed
-    __syncthreads();
+    float m = -INFINITY, l = 0.f;  // this warp's rows so far, head g (shared by the 4 t lanes)
     float o[16][4];
 #pragma unroll
-    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    for (int nn = 0; nn < 16; ++nn) o[nn][0] = o[nn][1] = o[nn][2] = o[nn][3] = 0.f;
     // ldmatrix.trans row addresses: matrix mi = lane / 8 = (keys half mi & 1, dims +8 (mi >> 1))
     const int mi = lane >> 3, mr = lane & 7;
-    const uint32_t vrow = sv + (uint32_t)(r0 + (mi & 1) * 8 + mr) * kAttnPitch + (mi >> 1) * 16;
+    const int r0 = warp * 16;
+    for (int c = c0; c < c1; ++c) {
+        const int stage = (c - c0) & 1;
+        const bool next = c + 1 < c1;  // chunk c+1's two groups are committed behind this one's
+        const uint32_t sk = s0 + stage * 2 * kAttnPTile, sv = sk + kAttnPTile;
+        if (next) asm volatile("cp.async.wait_group 3;" ::: "memory");  // K of chunk c landed
+        else asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();  // ... for every thread
+        float sc[2][4];
 #pragma unroll
-    for (int n = 0; n < 16; n += 2) {
-        uint32_t b00, b01, b10, b11;
-        ldsm_x4_trans(vrow + n * 16, b00, b01, b10, b11);
-        mma_16816(o[n], ph0, ph2, b00, b01);
-        mma_16816(o[n], pl0, pl2, b00, b01);
-        mma_16816(o[n + 1], ph0, ph2, b10, b11);
-        mma_16816(o[n + 1], pl0, pl2, b10, b11);
+        for (int nt = 0; nt < 2; ++nt) {
+            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+            const uint8_t* kr = s_tiles + (sk - s0) + (r0 + nt * 8 + g) * kAttnPitch + 4 * t;
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + 32 * ks);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + 32 * ks + 16);
+                mma_16816(sc[nt], qa[ks][0], qa[ks][1], b0, b1);
+            }
+        }
+        // this lane's scores of head g: keys r0 + 2t, r0 + 2t + 1, r0 + 8 + 2t, r0 + 9 + 2t
+        const int valid = (int)min((int64_t)kAttnChunk, pos + 1 - (int64_t)c * kAttnChunk);
+        float x[4] = {sc[0][0], sc[0][1], sc[1][0], sc[1][1]};
+        const int kk[4] = {r0 + 2 * t, r0 + 2 * t + 1, r0 + 8 + 2 * t, r0 + 9 + 2 * t};
+        float mc = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            x[i] = kk[i] < valid ? x[i] * scale : -INFINITY;
+            mc = fmaxf(mc, x[i]);
+        }
+        mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, 1));
+        mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, 2));
+        const float mn = fmaxf(m, mc);
+        const float alpha = m == mn ? 1.f : expf(m - mn);  // m = mn = -inf keeps o = l = 0
+        float p[4], lc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            p[i] = mn == -INFINITY ? 0.f : expf(x[i] - mn);  // 0 for rows past the position
+            lc += p[i];
+        }
+        lc += __shfl_xor_sync(0xffffffffu, lc, 1);
+        lc += __shfl_xor_sync(0xffffffffu, lc, 2);
+        l = l * alpha + lc;
+        m = mn;
+#pragma unroll
+        for (int nn = 0; nn < 16; ++nn) {
+            o[nn][0] *= alpha;
+            o[nn][1] *= alpha;
+        }
+        // P as A fragments, split into a bf16 high part and the bf16 rounding of the rest
+        const uint32_t ph0 = pack_bf16x2(p[0], p[1]), ph2 = pack_bf16x2(p[2], p[3]);
+        const uint32_t pl0 = pack_bf16x2(p[0] - bf16lo(ph0), p[1] - bf16hi(ph0));
+        const uint32_t pl2 = pack_bf16x2(p[2] - bf16lo(ph2), p[3] - bf16hi(ph2));
+
+        if (next) asm volatile("cp.async.wait_group 2;" ::: "memory");  // V of chunk c landed
+        else asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();
+        const uint32_t vrow = sv + (uint32_t)(r0 + (mi & 1) * 8 + mr) * kAttnPitch + (mi >> 1) * 16;
+#pragma unroll
+        for (int nn = 0; nn < 16; nn += 2) {
+            uint32_t b00, b01, b10, b11;
+            ldsm_x4_trans(vrow + nn * 16, b00, b01, b10, b11);
+            mma_16816(o[nn], ph0, ph2, b00, b01);
+            mma_16816(o[nn], pl0, pl2, b00, b01);
+            mma_16816(o[nn + 1], ph0, ph2, b10, b11);
+            mma_16816(o[nn + 1], pl0, pl2, b10, b11);
+        }
+        if (c + 2 < c1) {
+            __syncthreads();  // every warp is done with this stage
+            issue(c + 2, stage);
+        }
     }
-    __syncthreads();  // every warp is done with the K tile
+    __syncthreads();  // every warp is done with the tiles
     float* s_acc = reinterpret_cast<float*>(s_tiles);  // [4][G][128]
     if (g < G) {
 #pragma unroll
-        for (int n = 0; n < 16; ++n)
-            *reinterpret_cast<float2*>(s_acc + (warp * G + g) * kHeadDim + 8 * n + 2 * t) =
-                make_float2(o[n][0], o[n][1]);
+        for (int nn = 0; nn < 16; ++nn)
+            *reinterpret_cast<float2*>(s_acc + (warp * G + g) * kHeadDim + 8 * nn + 2 * t) =
+                make_float2(o[nn][0], o[nn][1]);
         if (t == 0) {
             s_m[warp][g] = m;
             s_l[warp][g] = l;
         }
     }
     __syncthreads();
-    // thread t combines element d = t of every query head of the group
+    // thread d combines element d of every query head of the group
     const int d = threadIdx.x;
 #pragma unroll
     for (int gg = 0; gg < G; ++gg) {
@@ -372,6 +418,34 @@ attn_partial_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
             part_ml[hrow * 2 + 1] = L;
         }
     }
+}
+
+// Splits per (kv head, sequence): as many as keep every CTA of the launch resident at once
+// (one wave), at most one per chunk of the cache.
+template <int G, int VB>
+static int attn_splits(int pairs, int chunks, int* splits) {
+    static int slots[64] = {};  // resident CTAs per device (0 = not yet counted)
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return NK_ERR_CUDA;
+    if (dev < 0 || dev >= 64) return NK_ERR_DEVICE;
+    if (slots[dev] == 0) {
+        int sms = 0, per_sm = 0;
+        if (cudaFuncSetAttribute(attn_partial_kernel<G, VB>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(attn_partial_kernel<G, VB>,
+                                 cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_partial_kernel<G, VB>,
+                                                          kAttnThreads, kAttnSmem) !=
+                cudaSuccess ||
+            per_sm < 1)
+            return NK_ERR_CUDA;
+        slots[dev] = sms * per_sm;
+    }
+    *splits = max(1, min(chunks, slots[dev] / pairs));
+    return NK_OK;
 }
 
 // One CTA per (sequence, query head); thread d owns output element d. The splits' maxima are
@@ -483,6 +557,36 @@ extern "C" int nk_qk_norm_rope_cache_bf16(const void* qkv, int64_t ld_qkv, const
         cache_head_stride, cache_seq_stride, eps);
 }
 
+struct AttnArgs {
+    const __nv_bfloat16 *q, *k_cache, *v_cache;
+    const int64_t* position;
+    __nv_bfloat16* out;
+    float* ws;
+    int batch, q_heads, kv_heads, chunks, capacity;
+    int64_t cb, ch, cs;
+    float scale;
+};
+
+// Partial kernel over `splits` CTAs per (kv head, sequence), then the merge. The partials sit
+// in the workspace as acc [batch][q_heads][splits][128], then (max, sum) [..][splits][2];
+// splits <= chunks, so they fit the workspace sized for one split per chunk.
+template <int G, int VB>
+static int launch_attention(const AttnArgs& a, cudaStream_t s) {
+    int splits = 0;
+    const int st = attn_splits<G, VB>(a.kv_heads * a.batch, a.chunks, &splits);
+    if (st != NK_OK) return st;
+    float* part_acc = a.ws;
+    float* part_ml = part_acc + (size_t)a.batch * a.q_heads * splits * kHeadDim;
+    const int rc = launch_pdl_smem(attn_partial_kernel<G, VB>, dim3(splits, a.kv_heads, a.batch),
+                                   dim3(kAttnThreads), (size_t)kAttnSmem, s, a.q, a.k_cache,
+                                   a.v_cache, a.position, part_acc, part_ml, a.q_heads,
+                                   a.kv_heads, splits, a.capacity, a.cb, a.ch, a.cs, a.scale);
+    if (rc != NK_OK) return rc;
+    return launch_pdl_smem(attn_merge_kernel, dim3(a.batch * a.q_heads), dim3(kHeadDim), 0, s,
+                           (const float*)part_acc, (const float*)part_ml, a.out, splits,
+                           a.capacity, a.position);
+}
+
 extern "C" size_t nk_attention_ws_bytes(int batch, int q_heads, int capacity) {
     if (batch < 1 || q_heads < 1 || capacity < 1) return 0;
     const size_t splits = (size_t)(capacity + kAttnChunk - 1) / kAttnChunk;
@@ -506,33 +610,23 @@ extern "C" int nk_attention_decode_bf16(const void* q, const void* k_cache, cons
     if (!al16(ws) || ((uintptr_t)q & 7u) || ((uintptr_t)k_cache & 7u) || ((uintptr_t)v_cache & 7u) ||
         (cache_seq_stride % 4) || (cache_head_stride % 4) || (cache_batch_stride % 4))
         return NK_ERR_ALIGN;
-    const int splits = (capacity + kAttnChunk - 1) / kAttnChunk;
-    float* part_acc = static_cast<float*>(ws);
-    float* part_ml = part_acc + (size_t)batch * q_heads * splits * kHeadDim;
-    cudaStream_t s = (cudaStream_t)stream;
-    const dim3 grid(splits, kv_heads, batch);
-    const auto* qq = static_cast<const __nv_bfloat16*>(q);
-    const auto* kk = static_cast<const __nv_bfloat16*>(k_cache);
-    const auto* vv = static_cast<const __nv_bfloat16*>(v_cache);
+    const int chunks = (capacity + kAttnChunk - 1) / kAttnChunk;
     // 16-byte copies when every cache row segment is 16-byte aligned, else 8-byte copies
     const bool wide = al16(k_cache) && al16(v_cache) && cache_seq_stride % 8 == 0 &&
                       cache_head_stride % 8 == 0 && cache_batch_stride % 8 == 0;
-    int st;
-#define NK_ATTN_LAUNCH(GG, VB)                                                                  \
-    launch_pdl_smem(attn_partial_kernel<GG, VB>, grid, dim3(kAttnThreads), 0, s, qq, kk, vv,    \
-                    position, part_acc, part_ml, q_heads, kv_heads, splits, capacity,           \
-                    cache_batch_stride, cache_head_stride, cache_seq_stride, scale)
+    const AttnArgs a{static_cast<const __nv_bfloat16*>(q),
+                     static_cast<const __nv_bfloat16*>(k_cache),
+                     static_cast<const __nv_bfloat16*>(v_cache), position,
+                     static_cast<__nv_bfloat16*>(out), static_cast<float*>(ws), batch, q_heads,
+                     kv_heads, chunks, capacity, cache_batch_stride, cache_head_stride,
+                     cache_seq_stride, scale};
+    cudaStream_t s = (cudaStream_t)stream;
     switch (G) {
-        case 1: st = wide ? NK_ATTN_LAUNCH(1, 16) : NK_ATTN_LAUNCH(1, 8); break;
-        case 2: st = wide ? NK_ATTN_LAUNCH(2, 16) : NK_ATTN_LAUNCH(2, 8); break;
-        case 4: st = wide ? NK_ATTN_LAUNCH(4, 16) : NK_ATTN_LAUNCH(4, 8); break;
-        default: st = wide ? NK_ATTN_LAUNCH(8, 16) : NK_ATTN_LAUNCH(8, 8); break;
+        case 1: return wide ? launch_attention<1, 16>(a, s) : launch_attention<1, 8>(a, s);
+        case 2: return wide ? launch_attention<2, 16>(a, s) : launch_attention<2, 8>(a, s);
+        case 4: return wide ? launch_attention<4, 16>(a, s) : launch_attention<4, 8>(a, s);
+        default: return wide ? launch_attention<8, 16>(a, s) : launch_attention<8, 8>(a, s);
     }
-#undef NK_ATTN_LAUNCH
-    if (st != NK_OK) return st;
-    return launch_pdl_smem(attn_merge_kernel, dim3(batch * q_heads), dim3(kHeadDim), 0, s,
-                           (const float*)part_acc, (const float*)part_ml,
-                           static_cast<__nv_bfloat16*>(out), splits, capacity, position);
 }
 
 extern "C" int nk_silu_mul_bf16(const void* gate_up, void* out, int rows, int intermediate,

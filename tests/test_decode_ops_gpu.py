@@ -123,6 +123,35 @@ def test_attention_decode(B, H, Hkv, cap):
             assert torch.equal(out2, out)
 
 
+@pytest.mark.parametrize("B,H,Hkv,cap", [(16, 32, 8, 1088), (32, 64, 8, 300), (8, 32, 8, 4160),
+                                         (40, 16, 8, 200)])
+def test_attention_decode_several_chunks_per_split(B, H, Hkv, cap):
+    """With many (sequence, kv head) pairs each split walks several chunks with the next one's
+    copies in flight (at 40 x 8 pairs every split covers the whole cache); positions where
+    the chunks divide unevenly over the splits, or number fewer than the splits."""
+    d = qwen3.Qwen3Dims(1024, 1024, H, Hkv, 128, 1, 64)
+    kc = rand(B, Hkv, cap, 128, seed=17)
+    vc = rand(B, Hkv, cap, 128, seed=18)
+    ws = ops.attention_workspace(B, H, cap, DEV)
+    slots = torch.arange(cap, device=DEV)
+    for pos in sorted({0, 65, 190, cap // 2 + 3, cap - 1}):
+        q = rand(B, H * 128, seed=300 + pos)
+        position = torch.tensor([pos], device=DEV)
+        out = torch.empty_like(q)
+        ops.attention_decode(q, kc, vc, position, out, ws, H, Hkv)
+        torch.cuda.synchronize()
+        ref = qwen3.attention(q.view(B, H, 128), kc, vc, position, slots, d)
+        close(out, ref, abs_slack=4e-3, exact_frac=0.97)
+        if pos + 1 < cap:
+            kp, vp = kc.clone(), vc.clone()
+            kp[:, :, pos + 1:] = float("nan")
+            vp[:, :, pos + 1:] = float("nan")
+            out2 = torch.empty_like(q)
+            ops.attention_decode(q, kp, vp, position, out2, ws, H, Hkv)
+            torch.cuda.synchronize()
+            assert torch.equal(out2, out)
+
+
 @pytest.mark.parametrize("H,Hkv", [(32, 8), (8, 1)])
 def test_attention_decode_8_byte_aligned_cache(H, Hkv):
     """Caches whose rows are only 8-byte aligned (row pitch 132 elements, base offset 4)
