@@ -18,10 +18,10 @@
 // stand-in), so the first call on each device, with that device current, looks the address
 // up with cudaGetSymbolAddress and keeps it; that first call on a device should therefore
 // come before any stream capture on it. Every call on a device shares the one array, which
-// keeps whatever the previous call left: each call clears the split-K tickets it will use
-// (the partial sums are always written before they are read), and calls whose executions
-// overlap on the GPU race on the array, so they must be ordered (one stream, or joined by
-// events).
+// keeps whatever the previous call left: each call first clears the part of the array its
+// plan uses (split-K tickets and partial slots, nk_ws_bytes of it), and calls whose
+// executions overlap on the GPU race on the array, so they must be ordered (one stream, or
+// joined by events).
 #include <mutex>
 
 #include "nk_common.cuh"
