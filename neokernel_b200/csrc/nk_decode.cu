@@ -215,8 +215,9 @@ __device__ __forceinline__ void attn_load_tile(uint32_t tile, const __nv_bfloat1
 
 __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0,
                                           uint32_t b1) {
-    // rows 8..15 of A are zero (at most 8 query heads per KV head)
-    asm volatile(
+    // rows 8..15 of A are zero (at most 8 query heads per KV head). Not volatile: a pure
+    // register operation, so the compiler may interleave independent accumulator chains.
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -374,8 +375,8 @@ attn_partial_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
             uint32_t b00, b01, b10, b11;
             ldsm_x4_trans(vrow + nn * 16, b00, b01, b10, b11);
             mma_16816(o[nn], ph0, ph2, b00, b01);
-            mma_16816(o[nn], pl0, pl2, b00, b01);
             mma_16816(o[nn + 1], ph0, ph2, b10, b11);
+            mma_16816(o[nn], pl0, pl2, b00, b01);
             mma_16816(o[nn + 1], pl0, pl2, b10, b11);
         }
         if (c + 2 < c1) {
@@ -448,39 +449,63 @@ static int attn_splits(int pairs, int chunks, int* splits) {
     return NK_OK;
 }
 
-// One CTA per (sequence, query head); thread d owns output element d. The splits' maxima are
-// gathered in parallel (one load per thread per 128 splits) and reduced across the CTA, then
-// the weighted sums run over the splits with their loads unrolled.
+// One CTA per (sequence, query head); thread d owns output element d. The splits are read in
+// batches of kMergeBatch with every load of a batch in flight at once (the first batch
+// together with the position, before the number of used splits is known: entries of
+// unused splits are read but ignored). Within a batch the weights use the batch's running
+// maximum; across batches the sums are rescaled, so up to kMergeBatch splits the result is
+// sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s with M the maximum over all splits.
+constexpr int kMergeBatch = 16;
+
 __global__ void __launch_bounds__(kHeadDim)
 attn_merge_kernel(const float* part_acc, const float* part_ml, __nv_bfloat16* out, int splits,
                   int capacity, const int64_t* position) {
-    __shared__ float s_max[kHeadDim / 32];
     if (threadIdx.x == 0) griddep_launch_dependents();
     griddep_wait();
     const int64_t hrow = blockIdx.x;  // b * Hq + h
     const int d = threadIdx.x;
-    const int64_t pos = min(*position, (int64_t)capacity - 1);
+    const float2* ml = reinterpret_cast<const float2*>(part_ml + hrow * splits * 2);
+    const float* pa = part_acc + hrow * splits * kHeadDim + d;
+    const int64_t pos_in = *position;
+    float2 v[kMergeBatch];
+    float acc[kMergeBatch];
+#pragma unroll
+    for (int j = 0; j < kMergeBatch; ++j) {
+        if (j < splits) {
+            v[j] = ml[j];
+            acc[j] = pa[(int64_t)j * kHeadDim];
+        }
+    }
+    const int64_t pos = min(pos_in, (int64_t)capacity - 1);
     if (pos < 0) return;  // no partials were written (the partial kernel flagged it)
     const int used = (int)min((int64_t)splits, pos / kAttnChunk + 1);
-    const float* ml = part_ml + hrow * splits * 2;
-    const float* pa = part_acc + hrow * splits * kHeadDim + d;
-    float M = -INFINITY;
-    for (int s = d; s < used; s += kHeadDim) M = fmaxf(M, ml[s * 2]);
-    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 16));
-    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 8));
-    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 4));
-    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 2));
-    M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 1));
-    if ((d & 31) == 0) s_max[d >> 5] = M;
-    __syncthreads();
-    M = fmaxf(fmaxf(s_max[0], s_max[1]), fmaxf(s_max[2], s_max[3]));
-    float L = 0.f, A = 0.f;
-#pragma unroll 8
-    for (int s = 0; s < used; ++s) {
-        const float ms = ml[s * 2];
-        const float f = ms == -INFINITY ? 0.f : expf(ms - M);
-        L += ml[s * 2 + 1] * f;
-        A += pa[(int64_t)s * kHeadDim] * f;
+    float M = -INFINITY, L = 0.f, A = 0.f;
+    for (int s0 = 0; s0 < used; s0 += kMergeBatch) {
+        if (s0 > 0) {
+#pragma unroll
+            for (int j = 0; j < kMergeBatch; ++j) {
+                if (s0 + j < used) {
+                    v[j] = ml[s0 + j];
+                    acc[j] = pa[(int64_t)(s0 + j) * kHeadDim];
+                }
+            }
+        }
+        float Mb = M;
+#pragma unroll
+        for (int j = 0; j < kMergeBatch; ++j)
+            if (s0 + j < used) Mb = fmaxf(Mb, v[j].x);
+        const float fo = M == Mb ? 1.f : expf(M - Mb);  // M = -inf: L = A = 0 either way
+        L *= fo;
+        A *= fo;
+#pragma unroll
+        for (int j = 0; j < kMergeBatch; ++j) {
+            if (s0 + j < used && v[j].x != -INFINITY) {
+                const float f = expf(v[j].x - Mb);
+                L += v[j].y * f;
+                A += acc[j] * f;
+            }
+        }
+        M = Mb;
     }
     out[hrow * kHeadDim + d] = __float2bfloat16_rn(A / L);
 }
