@@ -663,7 +663,8 @@ def attention_only(args):
 
 def decode_bench(nk, dev, batches, world, local, kv=1024, steps=20, warmup=3):
     """Decode tokens/s of the full Qwen3-8B step (36 layers, random init, CUDA graph) at KV
-    length 1024. Arms: the product (fused non-linear kernels + neokernel_b200.mm), the same
+    length 1024. Arms: the product (fused non-linear kernels, neokernel_b200.mm and the fused
+    lm_head + argmax), the same
     fused step with the linears on torch.mm (cuBLAS, the reference's call), and the step with
     PyTorch non-linear ops and torch.mm."""
     from neokernel_b200 import qwen3
@@ -676,7 +677,7 @@ def decode_bench(nk, dev, batches, world, local, kv=1024, steps=20, warmup=3):
         res = {}
         for B in batches:
             g = qwen3.GraphDecoder(w, B, kv + warmup + steps + 1, linear, device=dev,
-                                   fused=fused)
+                                   fused=fused, fused_head=linear is nk.mm)
             gen = torch.Generator(device=dev).manual_seed(B)
             for c in g.st.k_cache + g.st.v_cache:
                 c.normal_(generator=gen)

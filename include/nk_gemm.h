@@ -98,13 +98,14 @@ typedef struct nk_plan {
  */
 NK_API int nk_plan_make(nk_plan* plan, int M_max, int N, int K, int split_k, int kind);
 
-/* Bytes of device workspace nk_gemm_bf16 needs for this plan: a fixed 256 KiB region of
- * split-K tickets followed by the partial sums (8 bytes per partial value for the
- * tensor-core family, 4 for the GEMV family). 0 when the plan needs none (no tile is split).
- * One workspace (zeroed once by nk_ws_init) can serve any sequence of ordered calls whatever
- * their plans, if it is as large as the largest plan needs: every plan uses the same ticket
- * region and the kernels leave the tickets and the partial slots they read zeroed. Plans with split_k > 1 and more than 65536 output
- * tiles are refused (NK_ERR_SPLIT). */
+/* Bytes of device workspace nk_gemm_bf16 needs for this plan: a fixed 264 KiB region (256
+ * KiB of split-K tickets, then 8 KiB for nk_gemm_bf16_argmax's running maxima) followed by
+ * the partial sums (8 bytes per partial value for the tensor-core family, 4 for the GEMV
+ * family). 0 when the plan needs none (no tile is split). One workspace (zeroed once by
+ * nk_ws_init) can serve any sequence of ordered calls whatever their plans, if it is as large
+ * as the largest plan needs: every plan uses the same fixed regions and the kernels leave
+ * them, and the partial slots they read, zeroed. Plans with split_k > 1 and more than 65536
+ * output tiles are refused (NK_ERR_SPLIT). */
 NK_API size_t nk_ws_bytes(const nk_plan* plan);
 
 /* Zero a workspace once before its first use (the kernels keep it zeroed afterwards). After
@@ -164,6 +165,29 @@ NK_API int nk_gemm_bf16_static(const void* x, int64_t ldx,
 NK_API int nk_gemm_bf16_f32out(const void* x, int64_t ldx,
                                const void* w, int64_t ldw,
                                float* y32, int64_t ldy,
+                               int M, int N, int K,
+                               const nk_plan* plan, void* ws, size_t ws_bytes,
+                               nk_stream_t stream);
+
+/*
+ * Greedy head: y = x · Wᵀ as nk_gemm_bf16 and, per token m < M, idx[m] = the index n of the
+ * largest bf16 y[m, n], the lowest such n on ties (a NaN counts as the largest, -0 equals +0)
+ * — torch.argmax over the bf16 logits, fused into the linear's epilogue. Replaces
+ * engine/engine.py:114-116 (lm_head linear, then argmax(dim=-1)); lm_head + lowest-index
+ * argmax fusion is the reference's own next step for this path. y may be NULL: then no
+ * logits are written (ldy is ignored). best, if not NULL, receives each token's largest
+ * value (bf16, [M]). idx: int64 [M], 8-byte aligned.
+ * Tensor-core plans of at most 1016 tokens only (else NK_ERR_PLAN / NK_ERR_SHAPE; 0 from
+ * nk_gemm_argmax_ws_bytes). The workspace is the one nk_gemm_bf16 uses, at least
+ * nk_gemm_argmax_ws_bytes(plan) long — never 0, as the running maxima live in its fixed
+ * region — zeroed once by nk_ws_init; the kernel leaves it zeroed, so ordered calls of both
+ * entry points may share it.
+ */
+NK_API size_t nk_gemm_argmax_ws_bytes(const nk_plan* plan);
+NK_API int nk_gemm_bf16_argmax(const void* x, int64_t ldx,
+                               const void* w, int64_t ldw,
+                               void* y, int64_t ldy,
+                               int64_t* idx, void* best,
                                int M, int N, int K,
                                const nk_plan* plan, void* ws, size_t ws_bytes,
                                nk_stream_t stream);

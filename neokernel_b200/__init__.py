@@ -10,9 +10,9 @@ without it raises ImportError. There is no CPU or library fallback.
 
 from .gemm import (  # noqa: E402
     KIND_AUTO, KIND_GEMV, KIND_TC, KIND_GENERIC, Plan, device_error, linear_out, m_bucket, mm,
-    mm_f32, plan_for, workspace,
+    mm_argmax, mm_f32, plan_for, workspace,
 )
 
-__all__ = ["mm", "mm_f32", "linear_out", "Plan", "plan_for", "workspace", "device_error",
+__all__ = ["mm", "mm_argmax", "mm_f32", "linear_out", "Plan", "plan_for", "workspace", "device_error",
            "m_bucket", "KIND_AUTO", "KIND_GEMV", "KIND_TC", "KIND_GENERIC"]
 __version__ = "0.1.0"

@@ -39,7 +39,8 @@ EXPORTS = ("nk_plan_make", "nk_ws_bytes", "nk_ws_init", "nk_gemm_bf16", "nk_devi
            "nk_status_string", "nk_version", "nk_gemm_bf16_static", "nk_gemm_bf16_f32out",
            "nk_rmsnorm_bf16", "nk_qk_norm_rope_cache_bf16", "nk_attention_ws_bytes",
            "nk_attention_decode_bf16", "nk_silu_mul_bf16", "nk_peer_buffer_bytes", "nk_peer_alloc",
-           "nk_peer_free", "nk_ipc_handle", "nk_ipc_open", "nk_ipc_close", "nk_allreduce_bf16")
+           "nk_peer_free", "nk_ipc_handle", "nk_ipc_open", "nk_ipc_close", "nk_allreduce_bf16",
+           "nk_gemm_argmax_ws_bytes", "nk_gemm_bf16_argmax")
 
 
 NK_PEER_MAX_RANKS = 8
@@ -114,6 +115,11 @@ def load() -> ctypes.CDLL:
     L.nk_gemm_bf16_f32out.argtypes = [vp, i64, vp, i64, vp, i64, i32, i32, i32,
                                       ctypes.POINTER(NkPlan), vp, ctypes.c_size_t, vp]
     L.nk_gemm_bf16_f32out.restype = i32
+    L.nk_gemm_argmax_ws_bytes.argtypes = [ctypes.POINTER(NkPlan)]
+    L.nk_gemm_argmax_ws_bytes.restype = ctypes.c_size_t
+    L.nk_gemm_bf16_argmax.argtypes = [vp, i64, vp, i64, vp, i64, vp, vp, i32, i32, i32,
+                                      ctypes.POINTER(NkPlan), vp, ctypes.c_size_t, vp]
+    L.nk_gemm_bf16_argmax.restype = i32
     f32 = ctypes.c_float
     L.nk_rmsnorm_bf16.argtypes = [vp, vp, vp, vp, i32, i32, f32, vp]
     L.nk_rmsnorm_bf16.restype = i32

@@ -160,10 +160,17 @@ extern "C" int nk_ws_init(void* ws, size_t ws_bytes, nk_stream_t stream) {
 
 namespace nk {
 
-// Shared body of nk_gemm_bf16 (bf16 y) and nk_gemm_bf16_f32out (fp32 y).
+// Outputs of the greedy head (nk_gemm_bf16_argmax).
+struct AmaxOut {
+    int64_t* idx;
+    void* best;
+};
+
+// Shared body of nk_gemm_bf16 (bf16 y), nk_gemm_bf16_f32out (fp32 y) and
+// nk_gemm_bf16_argmax (bf16 y or none, plus the per-token argmax).
 static int gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
                      int64_t ldy, bool y_f32, int M, int N, int K, const nk_plan* p, void* ws,
-                     size_t ws_bytes, nk_stream_t stream);
+                     size_t ws_bytes, nk_stream_t stream, const AmaxOut* amax = nullptr);
 
 }  // namespace nk
 
@@ -181,12 +188,20 @@ extern "C" int nk_gemm_bf16_f32out(const void* x, int64_t ldx, const void* w, in
 
 static int nk::gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
                          int64_t ldy, bool y_f32, int M, int N, int K, const nk_plan* p,
-                         void* ws, size_t ws_bytes, nk_stream_t stream) {
+                         void* ws, size_t ws_bytes, nk_stream_t stream, const AmaxOut* amax) {
     if (!p || p->magic != NK_PLAN_MAGIC) return NK_ERR_PLAN;
     if (p->N != N || p->K != K) return NK_ERR_PLAN;
     if (M < 1 || M > p->M_max) return NK_ERR_SHAPE;
-    if (!x || !w || !y) return NK_ERR_ARG;
-    if (ldx < K || ldw < K || ldy < N) return NK_ERR_SHAPE;
+    if (!x || !w || (!y && !amax)) return NK_ERR_ARG;
+    if (ldx < K || ldw < K || (y && ldy < N)) return NK_ERR_SHAPE;
+    if (amax) {
+        if (p->kind != NK_KIND_TC) return NK_ERR_PLAN;  // the tensor-core family only
+        if (!amax->idx) return NK_ERR_ARG;
+        if (((uintptr_t)amax->idx & 7u) || ((uintptr_t)amax->best & 1u)) return NK_ERR_ALIGN;
+        if (p->M_max > kAmaxMaxTokens) return NK_ERR_SHAPE;
+        if (!ws || ws_bytes < amax_ws_bytes(*p)) return NK_ERR_WORKSPACE;
+        if (((uintptr_t)ws & 255u) != 0) return NK_ERR_ALIGN;
+    }
     if (!aligned2(x) || !aligned2(w) || !aligned2(y)) return NK_ERR_ALIGN;
     if (y_f32 && ((uintptr_t)y & 3u) != 0) return NK_ERR_ALIGN;
     if (p->kind == NK_KIND_GEMV || p->kind == NK_KIND_TC) {
@@ -210,6 +225,16 @@ static int nk::gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw,
     a.M = M; a.N = N; a.K = K;
     a.part = L.total ? reinterpret_cast<float*>(static_cast<char*>(ws) + L.part_offset) : nullptr;
     a.tickets = L.total ? static_cast<unsigned*>(ws) : nullptr;
+    a.amax_keys = nullptr;
+    a.amax_done = nullptr;
+    a.amax_idx = nullptr;
+    a.amax_best = nullptr;
+    if (amax) {
+        a.amax_keys = reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + kAmaxOffset);
+        a.amax_done = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + kAmaxCountOffset);
+        a.amax_idx = amax->idx;
+        a.amax_best = static_cast<__nv_bfloat16*>(amax->best);
+    }
 
     cudaStream_t s = (cudaStream_t)stream;
     switch (p->kind) {
@@ -218,6 +243,20 @@ static int nk::gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw,
         case NK_KIND_TC: return launch_tc(*p, a, s);
         default: return NK_ERR_PLAN;
     }
+}
+
+extern "C" size_t nk_gemm_argmax_ws_bytes(const nk_plan* p) {
+    if (!p || p->magic != NK_PLAN_MAGIC || p->kind != NK_KIND_TC) return 0;
+    if (p->M_max > kAmaxMaxTokens) return 0;
+    return amax_ws_bytes(*p);
+}
+
+extern "C" int nk_gemm_bf16_argmax(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                   void* y, int64_t ldy, int64_t* idx, void* best, int M, int N,
+                                   int K, const nk_plan* p, void* ws, size_t ws_bytes,
+                                   nk_stream_t stream) {
+    const AmaxOut out{idx, best};
+    return gemm_impl(x, ldx, w, ldw, y, ldy, false, M, N, K, p, ws, ws_bytes, stream, &out);
 }
 
 extern "C" int nk_device_error(nk_stream_t stream, int* status) {

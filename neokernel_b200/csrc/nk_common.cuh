@@ -142,13 +142,20 @@ __device__ __forceinline__ void splitk_reduce_tile(const GemmArgsT& a, int n_bas
 }
 
 // Workspace layout: a fixed region of kTicketsMax split-K tickets at offset 0, then the
-// partials — [split][M_max][N] fp32 for the GEMV family, [tile][segment][token column][128
-// rows] 64-bit slots for the tensor-core family. Every plan puts its tickets in the same fixed
-// region, the kernels leave the tickets at zero and clear every tagged slot they read, so any
-// sequence of ordered calls may share one workspace whatever their plans (one plan's
-// partials never overlay another's tickets).
+// greedy head's fixed region (the running (value, index) keys of up to kAmaxMaxTokens tokens
+// and a count of finished CTAs), then the partials — [split][M_max][N] fp32 for the GEMV
+// family, [tile][segment][token column][128 rows] 64-bit slots for the tensor-core family.
+// Every plan puts its tickets and keys in the same fixed regions, the kernels leave tickets,
+// keys and count at zero and clear every tagged slot they read, so any sequence of ordered
+// calls may share one workspace whatever their plans (one plan's partials never overlay
+// another's tickets or keys).
 constexpr size_t kTicketsMax = 65536;
 constexpr size_t kTicketBytes = kTicketsMax * sizeof(unsigned);
+constexpr size_t kAmaxOffset = kTicketBytes;
+constexpr size_t kAmaxBytes = 8192;
+constexpr int kAmaxMaxTokens = (int)((kAmaxBytes - 64) / sizeof(uint64_t));  // 1016
+constexpr size_t kAmaxCountOffset = kAmaxOffset + kAmaxBytes - 64;
+constexpr size_t kPartOffset = kAmaxOffset + kAmaxBytes;
 
 struct WsLayout {
     size_t part_offset;
@@ -160,7 +167,7 @@ struct WsLayout {
 inline WsLayout ws_layout(const nk_plan& p) {
     WsLayout L{};
     L.ticket_count = (size_t)p.n_tiles * (size_t)p.m_tiles;
-    L.part_offset = kTicketBytes;
+    L.part_offset = kPartOffset;
     if (p.kind == NK_KIND_TC) {
         // [tile][segment][token column][128 rows] 64-bit {fp32 value, tag} slots, only when
         // some tile is shared
@@ -174,6 +181,13 @@ inline WsLayout ws_layout(const nk_plan& p) {
     }
     L.total = L.part_offset + ((L.part_bytes + 255) & ~(size_t)255);
     return L;
+}
+
+// Workspace bytes the greedy head (nk_gemm_bf16_argmax) needs: the plan's, and at least the
+// fixed regions in front of the partials.
+inline size_t amax_ws_bytes(const nk_plan& p) {
+    const size_t t = ws_layout(p).total;
+    return t > kPartOffset ? t : kPartOffset;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -223,6 +237,11 @@ struct GemmArgs {
     int part_cols;          // token columns per partial slot (min(NT, M_max))
     int coresident;         // 1: every CTA of the grid is resident at once (see nk_tc.cu)
     TcPartition part_map;
+    // greedy head (nk_gemm_bf16_argmax) only; all nullptr otherwise
+    unsigned long long* amax_keys;  // [M] (ordered value, inverted index) keys, zero between calls
+    unsigned* amax_done;            // CTAs that have folded their rows in, zero between calls
+    int64_t* amax_idx;              // [M] lowest index of each token's largest bf16 output
+    __nv_bfloat16* amax_best;       // [M] that largest value, or nullptr
 };
 
 int launch_gemv(const nk_plan& p, const GemmArgs& a, cudaStream_t s);

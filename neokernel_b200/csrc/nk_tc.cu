@@ -344,6 +344,44 @@ __device__ __forceinline__ bool collect_partials16(uint64_t* slot0, int part_col
     return collect_rounds<4, 4>(slot0, part_cols, c0, nseg, mcount, ps);
 }
 
+// Greedy head: a token's best output is its largest bf16 value, the lowest vocabulary index
+// on ties (torch.argmax over the bf16 logits; a NaN counts as the largest, -0 equals +0). The
+// key packs an order-preserving 16-bit image of the bf16 value above the inverted index, so
+// the largest key is that (value, index); a valid key is never zero.
+__device__ __forceinline__ unsigned long long amax_key(float v, int n) {
+    uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    if (h == 0x8000u) h = 0u;
+    uint32_t o;
+    if ((h & 0x7FFFu) > 0x7F80u) o = 0xFFFFu;
+    else o = (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
+    return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)n);
+}
+
+__device__ __forceinline__ __nv_bfloat16 amax_value(unsigned long long k) {
+    const uint32_t o = (uint32_t)(k >> 32);
+    const uint32_t h = o == 0xFFFFu ? 0x7FC0u : (o & 0x8000u) ? (o & 0x7FFFu) : (~o & 0xFFFFu);
+    return __ushort_as_bfloat16((unsigned short)h);
+}
+
+// Folds one 16-column chunk of this thread's output row n (values v, tokens m..m+cols-1) into
+// the tokens' keys: a warp-wide maximum per column, then one atomicMax per warp. Every lane of
+// the warp calls it; `live` is false for a lane whose row is past N or whose values are not
+// final. cols is warp-uniform.
+__device__ __forceinline__ void amax_fold16(const GemmArgs& a, bool live, int n, int m, int cols,
+                                            const float (&v)[16]) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        if (j >= cols) break;
+        unsigned long long k = live ? amax_key(v[j], n) : 0ull;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, off);
+            k = o > k ? o : k;
+        }
+        if ((threadIdx.x & 31) == 0 && k != 0ull) atomicMax(a.amax_keys + m + j, k);
+    }
+}
+
 // One tile segment of this CTA's unit range.
 struct Segment {
     int t;         // tile index
@@ -364,7 +402,9 @@ __device__ __forceinline__ Segment segment_at(int64_t u, int64_t u_end, int KB) 
 // warps per SM need at most 128 registers a thread (each SM sub-partition holds up to four
 // of the twelve warps), hence the cap for the token tiles that fit twice in shared memory.
 #define NK_TC_MAXNREG 128
-template <int NT>
+// AMAX: the greedy-head variant (nk_gemm_bf16_argmax) — folds every final output into the
+// tokens' (value, index) keys and may skip storing y; the plain variant compiles without it.
+template <int NT, bool AMAX>
 __global__ void __launch_bounds__(kTcThreads) __maxnreg__(NT <= 64 ? NK_TC_MAXNREG : 255)
 tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
           GemmArgs a) {
@@ -522,6 +562,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
         const uint32_t tlane = (uint32_t)(32 * q) << 16;
         const bool wait_mode = a.coresident != 0;
         const bool tagged = wait_mode && a.M <= NK_TC_TAG_MAX_M;  // the same for every CTA
+        const bool store_y = !AMAX || a.y != nullptr;            // the greedy head may skip y
         int seg = 0;
         for (int64_t u = u_begin; u < u_end; ++seg) {
             const Segment sg = segment_at(u, u_end, KB);
@@ -578,12 +619,13 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                         if (c0 >= mcount) break;  // warp-uniform
                         float v[16];
                         tmem_ld16(taddr + c0, v);
-                        if (n < a.N) {
+                        if (store_y && n < a.N) {
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
                                 if (c0 + j < mcount)
                                     store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n, v[j]);
                         }
+                        if constexpr (AMAX) amax_fold16(a, n < a.N, n, m0 + c0, min(16, mcount - c0), v);
                     }
                 }
             } else if (!finisher) {
@@ -648,12 +690,17 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                         for (int i = 0; i < partners; ++i)
 #pragma unroll
                             for (int j = 0; j < 16; ++j) ps[j] += sm[(i * 16 + j) * kTcRows];
-                        if (arrived && n < a.N) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] += ps[j];
+                        if (store_y && arrived && n < a.N) {
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
                                 if (16 * k + j < mcount)
-                                    store_out(a, (int64_t)(m0 + 16 * k + j) * a.ldy + n, v[j] + ps[j]);
+                                    store_out(a, (int64_t)(m0 + 16 * k + j) * a.ldy + n, v[j]);
                         }
+                        if constexpr (AMAX)
+                            amax_fold16(a, arrived && n < a.N, n, m0 + 16 * k,
+                                        min(16, mcount - 16 * k), v);
                         epi_bar();  // every thread is done with this half
                         if (ep == 0 && k + 2 < nchunks) {
                             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -673,12 +720,16 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                         }
                         float v[16];
                         tmem_ld16(taddr + c0, v);
-                        if (got && n < a.N) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] += psum[j];
+                        if (store_y && got && n < a.N) {
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
                                 if (c0 + j < mcount)
-                                    store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n, v[j] + psum[j]);
+                                    store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n, v[j]);
                         }
+                        if constexpr (AMAX)
+                            amax_fold16(a, got && n < a.N, n, m0 + c0, min(16, mcount - c0), v);
                     }
                 }
                 if (!tagged && ep == 0) a.tickets[sg.t] = 0u;  // re-armed for the next launch
@@ -703,22 +754,44 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                 epi_bar();
                 if (*last_flag) {
                     __threadfence();
-                    if (n < a.N && *abort_flag == 0u) {
-                        for (int c0 = 0; c0 < mcount; c0 += 16) {
-                            float ps[16];
+                    const bool live = n < a.N && *abort_flag == 0u;
+                    for (int c0 = 0; c0 < mcount; c0 += 16) {
+                        float ps[16];
 #pragma unroll
-                            for (int j = 0; j < 16; ++j) ps[j] = 0.f;
+                        for (int j = 0; j < 16; ++j) ps[j] = 0.f;
+                        if (live) {
                             sum_partials16(part0, a.part_cols, c0, nseg, mcount, ps);
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
-                                if (c0 + j < mcount)
-                                    store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n,
-                                              __ldcg(part0 + ((size_t)c0 + j) * kTcRows) + ps[j]);
+                                if (c0 + j < mcount) {
+                                    ps[j] += __ldcg(part0 + ((size_t)c0 + j) * kTcRows);
+                                    if (store_y)
+                                        store_out(a, (int64_t)(m0 + c0 + j) * a.ldy + n, ps[j]);
+                                }
                         }
+                        if constexpr (AMAX)
+                            amax_fold16(a, live, n, m0 + c0, min(16, mcount - c0), ps);
                     }
                     if (ep == 0) a.tickets[sg.t] = 0u;  // re-armed for the next launch
                 }
                 epi_bar();  // last_flag is rewritten by the next partial segment
+            }
+        }
+        if constexpr (AMAX) {
+            // The CTA whose arrival completes the count turns the keys into indices and
+            // leaves keys and count zero for the next call.
+            __threadfence();  // this thread's key updates, before the CTA's arrival
+            epi_bar();
+            if (ep == 0) *last_flag = atomicAdd(a.amax_done, 1u) == gridDim.x - 1 ? 1u : 0u;
+            epi_bar();
+            if (*last_flag) {
+                __threadfence();
+                for (int m = ep; m < a.M; m += kTcEpiThreads) {
+                    const unsigned long long k = atomicExch(a.amax_keys + m, 0ull);
+                    a.amax_idx[m] = k ? (int64_t)(0xFFFFFFFFu - (uint32_t)k) : (int64_t)-1;
+                    if (a.amax_best) a.amax_best[m] = amax_value(k);
+                }
+                if (ep == 0) atomicExch(a.amax_done, 0u);
             }
         }
     }
@@ -805,18 +878,18 @@ int tc_ctas_per_sm(int nt) {
     }
 }
 
-// CTAs of tc_kernel<NT> that fit on one SM at once. The runtime's occupancy query answers 1
+// CTAs of tc_kernel<NT, AMAX> that fit on one SM at once. The runtime's occupancy query answers 1
 // for every kernel that executes tcgen05.alloc (on B200 even for a 12-register kernel), but
 // the block scheduler places such CTAs by registers, shared memory and threads: 296 CTAs
 // that each hold 32 TMEM columns run on 148 SMs as one wave, two overlapping on every SM.
 // So the count is made here from those limits, plus the 512 TMEM columns of an SM (so no
 // CTA blocks in tcgen05.alloc), and capped at the per-SM count the stage budget assumes.
-template <int NT>
+template <int NT, bool AMAX>
 static int tc_resident_per_sm(int dev) {
     using L = TcSmem<NT>;
     cudaFuncAttributes fa;
     int smem_sm = 0, reserved = 0, regs_sm = 0, thr_sm = 0;
-    if (cudaFuncGetAttributes(&fa, tc_kernel<NT>) != cudaSuccess ||
+    if (cudaFuncGetAttributes(&fa, tc_kernel<NT, AMAX>) != cudaSuccess ||
         cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) !=
             cudaSuccess ||
         cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) !=
@@ -839,7 +912,7 @@ static int tc_resident_per_sm(int dev) {
     return n;
 }
 
-template <int NT>
+template <int NT, bool AMAX>
 static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
                        const CUtensorMap& mx, cudaStream_t s) {
     using L = TcSmem<NT>;
@@ -848,15 +921,15 @@ static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
     if (cudaGetDevice(&dev) != cudaSuccess) return NK_ERR_CUDA;
     if (dev < 0 || dev >= 64) return NK_ERR_DEVICE;
     if (resident[dev] == 0) {
-        if (cudaFuncSetAttribute(tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(tc_kernel<NT, AMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  L::kAlloc) != cudaSuccess ||
-            cudaFuncSetAttribute(tc_kernel<NT>, cudaFuncAttributePreferredSharedMemoryCarveout,
+            cudaFuncSetAttribute(tc_kernel<NT, AMAX>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return NK_ERR_CUDA;
         int sms = 0;
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
             return NK_ERR_CUDA;
-        const int per_sm = tc_resident_per_sm<NT>(dev);
+        const int per_sm = tc_resident_per_sm<NT, AMAX>(dev);
         if (per_sm < 1) return NK_ERR_CUDA;
         resident[dev] = per_sm * sms;
     }
@@ -887,7 +960,7 @@ static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = NK_PDL ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, tc_kernel<NT>, mw, mx, a) == cudaSuccess ? NK_OK
+    return cudaLaunchKernelEx(&cfg, tc_kernel<NT, AMAX>, mw, mx, a) == cudaSuccess ? NK_OK
                                                                                       : NK_ERR_CUDA;
 }
 
@@ -908,12 +981,18 @@ int launch_tc(const nk_plan& p, const GemmArgs& in, cudaStream_t s) {
     CUtensorMap mw, mx;
     if (make_map(&mw, a.w, a.N, a.K, a.ldw, kTcRows) != NK_OK) return NK_ERR_ALIGN;
     if (make_map(&mx, a.x, a.M, a.K, a.ldx, nt) != NK_OK) return NK_ERR_ALIGN;
+    const bool amax = a.amax_keys != nullptr;
     switch (nt) {
-        case 16: return launch_tc_t<16>(p, a, mw, mx, s);
-        case 32: return launch_tc_t<32>(p, a, mw, mx, s);
-        case 64: return launch_tc_t<64>(p, a, mw, mx, s);
-        case 128: return launch_tc_t<128>(p, a, mw, mx, s);
-        case 256: return launch_tc_t<256>(p, a, mw, mx, s);
+        case 16: return amax ? launch_tc_t<16, true>(p, a, mw, mx, s)
+                       : launch_tc_t<16, false>(p, a, mw, mx, s);
+        case 32: return amax ? launch_tc_t<32, true>(p, a, mw, mx, s)
+                       : launch_tc_t<32, false>(p, a, mw, mx, s);
+        case 64: return amax ? launch_tc_t<64, true>(p, a, mw, mx, s)
+                       : launch_tc_t<64, false>(p, a, mw, mx, s);
+        case 128: return amax ? launch_tc_t<128, true>(p, a, mw, mx, s)
+                       : launch_tc_t<128, false>(p, a, mw, mx, s);
+        case 256: return amax ? launch_tc_t<256, true>(p, a, mw, mx, s)
+                       : launch_tc_t<256, false>(p, a, mw, mx, s);
         default: return NK_ERR_PLAN;
     }
 }

@@ -192,6 +192,75 @@ def _mm(a, b, out, plan, stream, f32):
     return out
 
 
+def mm_argmax(a: torch.Tensor, b: torch.Tensor, *, idx: torch.Tensor,
+              logits: torch.Tensor | None = None, best: torch.Tensor | None = None,
+              plan: Plan | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """Greedy head: ``idx[m] = argmax_n (a @ b)[m, n]`` over the bf16 products, lowest index on
+    ties — ``torch.mm(a, b, out=logits); torch.argmax(logits, dim=-1, out=idx)`` at
+    engine/engine.py:114-116 in one launch, the argmax folded into the linear's epilogue.
+
+    a: bf16 CUDA [M, K]; b = W.t() of a row-major [N, K] weight (as ``mm``); idx: int64 CUDA
+    [M]. ``logits`` (bf16 [M, N], unit column stride) is written only if given, so the
+    [M, N] logits need not be stored; ``best`` (bf16 [M]) receives each row's maximum.
+    Tensor-core plans only (16-byte aligned operands, K a multiple of 8).
+    """
+    _check_tensor(a, "a")
+    _check_tensor(b, "b")
+    M, K = a.shape
+    K2, N = b.shape
+    if K2 != K:
+        raise ValueError(f"mm_argmax: a is [{M}, {K}] but b is [{K2}, {N}]")
+    if not isinstance(idx, torch.Tensor) or idx.dtype != torch.int64 or idx.device != a.device:
+        raise ValueError("mm_argmax: idx must be an int64 tensor on a's device")
+    if idx.dim() != 1 or idx.shape[0] != M or (M > 1 and idx.stride(0) != 1):
+        raise ValueError(f"mm_argmax: idx must be a contiguous [{M}] tensor")
+    if logits is not None:
+        _check_tensor(logits, "logits")
+        if tuple(logits.shape) != (M, N) or (N > 1 and logits.stride(1) != 1):
+            raise ValueError(f"mm_argmax: logits must be [{M}, {N}] with unit stride along N")
+    if best is not None:
+        if (best.dtype != torch.bfloat16 or best.device != a.device or best.dim() != 1
+                or best.shape[0] != M or (M > 1 and best.stride(0) != 1)):
+            raise ValueError(f"mm_argmax: best must be a contiguous bf16 [{M}] tensor")
+    if b.device != a.device:
+        raise ValueError("mm_argmax: a and b must be on the same device")
+    if M == 0:
+        return idx
+    if N == 0 or K == 0:
+        raise ValueError("mm_argmax: needs N >= 1 and K >= 1")
+    if a.stride(1) != 1 and K > 1:
+        raise ValueError("mm_argmax: a must have unit stride along K")
+    if b.stride(0) != 1 and K > 1:
+        raise ValueError("mm_argmax: b must be the transposed view W.t() of a row-major "
+                         "[N, K] weight (strides (1, ldw))")
+    ldx = a.stride(0) if M > 1 else K
+    ldw = b.stride(1) if N > 1 else K
+    ldy = (logits.stride(0) if M > 1 else N) if logits is not None else 0
+    if plan is None:
+        plan = plan_for(M, N, K)
+    L = _lib.load()
+    need = int(L.nk_gemm_argmax_ws_bytes(plan._ref))
+    if need == 0:
+        raise ValueError("mm_argmax: the plan is not a tensor-core plan (operands must be "
+                         "16-byte aligned with K a multiple of 8)")
+    dev = a.device
+    if stream is None:
+        stream = torch.cuda.current_stream(dev)
+    ws = workspace(need, dev, stream)
+    args = (a.data_ptr(), ldx, b.data_ptr(), ldw,
+            logits.data_ptr() if logits is not None else None, ldy, idx.data_ptr(),
+            best.data_ptr() if best is not None else None, M, N, K, plan._ref, ws.data_ptr(),
+            ws.numel(), stream.cuda_stream)
+    if dev.index != torch.cuda.current_device():
+        with torch.cuda.device(dev):
+            status = L.nk_gemm_bf16_argmax(*args)
+    else:
+        status = L.nk_gemm_bf16_argmax(*args)
+    if status != _lib.NK_OK:
+        _raise(status, f"nk_gemm_bf16_argmax(M={M}, N={N}, K={K})")
+    return idx
+
+
 def linear_out(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor,
                plan: Plan | None = None) -> torch.Tensor:
     """``out = x · weightᵀ`` for a row-major [N, K] ``weight`` (same as ``mm(x, weight.t(), out=out)``)."""

@@ -226,6 +226,14 @@ def greedy_head(st: DecodeState, lm_head, linear):
     torch.argmax(st.logits, dim=-1, out=st.next_tokens)                  # lowest index on ties
 
 
+def fused_greedy_head(st: DecodeState, lm_head, linear):
+    """lm_head and the lowest-index argmax in one launch (nk_gemm_bf16_argmax,
+    engine.py:114-116): ``next_tokens`` without storing the [B, vocab] logits, so
+    ``st.logits`` is left untouched."""
+    from . import gemm
+    gemm.mm_argmax(st.norm, lm_head, idx=st.next_tokens)
+
+
 def decode_step(st: DecodeState, w: Qwen3Weights, linear, row_linear=None, head=None,
                 fused=False):
     """One greedy decode step for every sequence at ``st.position``; writes ``st.next_tokens``.
@@ -257,13 +265,16 @@ class GraphDecoder:
     engine/engine.py:119-129: side-stream warm-up x3, then capture) and replayed per token."""
 
     def __init__(self, w: Qwen3Weights, batch: int, capacity: int, linear, device="cuda",
-                 make_hooks=None, fused=False):
+                 make_hooks=None, fused=False, fused_head=False):
         """``make_hooks(state) -> (row_linear, head)`` supplies the tensor-parallel hooks,
         built once per state so their buffers are fixed before capture; ``fused`` selects the
-        fused CUDA kernels for the non-linear ops."""
+        fused CUDA kernels for the non-linear ops; ``fused_head`` the lm_head + argmax launch
+        (no logits are stored, so ``teacher_forced_logits`` needs it off)."""
         self.w, self.linear = w, linear
         self.st = DecodeState(w, batch, capacity, device)
         row_linear, head = make_hooks(self.st) if make_hooks else (None, None)
+        if fused_head and head is None:
+            head = fused_greedy_head
         step = lambda: decode_step(self.st, w, linear, row_linear, head, fused)  # noqa: E731
         stream = torch.cuda.Stream(device=device)
         self.stream = stream

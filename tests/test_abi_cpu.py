@@ -238,3 +238,32 @@ def test_python_shim_rejects_cpu_tensors():
 def test_m_bucket():
     assert [nk.m_bucket(m) for m in (1, 2, 3, 4, 5, 8, 9, 16, 17, 64, 100, 256)] == \
         [1, 2, 4, 4, 8, 8, 16, 16, 32, 64, 112, 256]
+
+
+def test_argmax_entry_rejects_before_launch():
+    L = _lib.load()
+    st, p = make(16, 151936, 4096)
+    assert st == 0 and p.kind == _lib.KIND_TC
+    need = L.nk_gemm_argmax_ws_bytes(ctypes.byref(p))
+    assert need >= 264 * 1024 and need >= L.nk_ws_bytes(ctypes.byref(p)) and need % 256 == 0
+    st, g = make(4, 4096, 1024, 0, _lib.KIND_GEMV)
+    assert st == 0 and L.nk_gemm_argmax_ws_bytes(ctypes.byref(g)) == 0
+    st, big = make(1024, 4096, 4096)
+    assert st == 0 and L.nk_gemm_argmax_ws_bytes(ctypes.byref(big)) == 0  # > 1016 tokens
+
+    def am(plan, y=0x30000, idx=0x50000, best=None, M=1, ws=0x100000, ws_bytes=need):
+        return L.nk_gemm_bf16_argmax(0x10000, plan.K, 0x20000, plan.K, y, plan.N, idx, best,
+                                     M, plan.N, plan.K, ctypes.byref(plan), ws, ws_bytes, None)
+
+    assert am(g) == _lib.NK_ERR_PLAN
+    assert am(big, M=1) == _lib.NK_ERR_SHAPE
+    assert am(p, idx=None) == _lib.NK_ERR_ARG
+    assert am(p, idx=0x50004) == _lib.NK_ERR_ALIGN
+    assert am(p, best=0x60001) == _lib.NK_ERR_ALIGN
+    assert am(p, ws=None) == _lib.NK_ERR_WORKSPACE
+    assert am(p, ws_bytes=need - 1) == _lib.NK_ERR_WORKSPACE
+    assert am(p, ws=0x100010) == _lib.NK_ERR_ALIGN
+    assert am(p, M=17) == _lib.NK_ERR_SHAPE
+    # no logits: y may be NULL, but nk_gemm_bf16 itself still needs y
+    assert am(p, y=None, ws=0x100010) == _lib.NK_ERR_ALIGN
+    assert call(p, y=0) == _lib.NK_ERR_ARG
