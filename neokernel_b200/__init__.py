@@ -13,6 +13,6 @@ from .gemm import (  # noqa: E402
     mm_argmax, mm_f32, plan_for, workspace,
 )
 
-__all__ = ["mm", "mm_argmax", "mm_f32", "linear_out", "Plan", "plan_for", "workspace", "device_error",
-           "m_bucket", "KIND_AUTO", "KIND_GEMV", "KIND_TC", "KIND_GENERIC"]
+__all__ = ["mm", "mm_argmax", "mm_f32", "linear_out", "Plan", "plan_for", "workspace",
+           "device_error", "m_bucket", "KIND_AUTO", "KIND_GEMV", "KIND_TC", "KIND_GENERIC"]
 __version__ = "0.1.0"
