@@ -26,7 +26,8 @@ def rand(*shape, std=1.0, seed=0):
 
 
 SHAPES = [(1, 151936, 4096), (4, 151936, 4096), (16, 151936, 4096), (3, 1000, 256),
-          (7, 129, 4096), (64, 50000, 1024), (128, 9000, 512), (200, 4096, 1024)]
+          (7, 129, 4096), (64, 50000, 1024), (128, 9000, 512), (200, 4096, 1024),
+          (4, 75968, 4096), (8, 37984, 5120), (1, 18992, 5120)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
