@@ -763,7 +763,8 @@ def decode_step_only(args, kv=1024):
     dev = torch.device("cuda", 0)
     B = args.decode_step
     w = qwen3.Qwen3Weights(qwen3.QWEN3_8B, seed=7, device=dev)
-    g = qwen3.GraphDecoder(w, B, kv + args.reps + 1, nk.mm, device=dev, fused=True)
+    g = qwen3.GraphDecoder(w, B, kv + args.reps + 1, nk.mm, device=dev, fused=True,
+                           fused_head=True)
     g.st.position.fill_(kv)
     for _ in range(args.reps):
         g.step()
