@@ -98,8 +98,8 @@ typedef struct nk_plan {
  */
 NK_API int nk_plan_make(nk_plan* plan, int M_max, int N, int K, int split_k, int kind);
 
-/* Bytes of device workspace nk_gemm_bf16 needs for this plan: a fixed 264 KiB region (256
- * KiB of split-K tickets, then 8 KiB for nk_gemm_bf16_argmax's running maxima) followed by
+/* Bytes of device workspace nk_gemm_bf16 needs for this plan: a fixed 288 KiB region (256
+ * KiB of split-K tickets, then 32 KiB for nk_gemm_bf16_argmax's running maxima) followed by
  * the partial sums (8 bytes per partial value for the tensor-core family, 4 for the GEMV
  * family). 0 when the plan needs none (no tile is split). One workspace (zeroed once by
  * nk_ws_init) can serve any sequence of ordered calls whatever their plans, if it is as large
@@ -177,7 +177,7 @@ NK_API int nk_gemm_bf16_f32out(const void* x, int64_t ldx,
  * argmax fusion is the reference's own next step for this path. y may be NULL: then no
  * logits are written (ldy is ignored). best, if not NULL, receives each token's largest
  * value (bf16, [M]). idx: int64 [M], 8-byte aligned.
- * Tensor-core plans of at most 1016 tokens only (else NK_ERR_PLAN / NK_ERR_SHAPE; 0 from
+ * Tensor-core plans of at most 255 tokens only (else NK_ERR_PLAN / NK_ERR_SHAPE; 0 from
  * nk_gemm_argmax_ws_bytes). The workspace is the one nk_gemm_bf16 uses, at least
  * nk_gemm_argmax_ws_bytes(plan) long — never 0, as the running maxima live in its fixed
  * region — zeroed once by nk_ws_init; the kernel leaves it zeroed, so ordered calls of both

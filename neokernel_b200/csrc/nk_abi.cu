@@ -230,7 +230,8 @@ static int nk::gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw,
     a.amax_idx = nullptr;
     a.amax_best = nullptr;
     if (amax) {
-        a.amax_keys = reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + kAmaxOffset);
+        a.amax_keys =  // keys kAmaxKeyStride bytes apart
+            reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + kAmaxOffset);
         a.amax_done = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + kAmaxCountOffset);
         a.amax_idx = amax->idx;
         a.amax_best = static_cast<__nv_bfloat16*>(amax->best);

@@ -151,10 +151,14 @@ __device__ __forceinline__ void splitk_reduce_tile(const GemmArgsT& a, int n_bas
 // another's tickets or keys).
 constexpr size_t kTicketsMax = 65536;
 constexpr size_t kTicketBytes = kTicketsMax * sizeof(unsigned);
+// One 128-byte line per token key: every warp of every tile updates each token's key, and
+// atomics on keys sharing a line queue behind one another in its L2 slice (16 keys in one
+// line cost lm_head at 16 tokens ~80 us).
 constexpr size_t kAmaxOffset = kTicketBytes;
-constexpr size_t kAmaxBytes = 8192;
-constexpr int kAmaxMaxTokens = (int)((kAmaxBytes - 64) / sizeof(uint64_t));  // 1016
-constexpr size_t kAmaxCountOffset = kAmaxOffset + kAmaxBytes - 64;
+constexpr size_t kAmaxKeyStride = 128;
+constexpr int kAmaxMaxTokens = 255;
+constexpr size_t kAmaxBytes = (kAmaxMaxTokens + 1) * kAmaxKeyStride;  // 32 KiB: keys, count
+constexpr size_t kAmaxCountOffset = kAmaxOffset + kAmaxMaxTokens * kAmaxKeyStride;
 constexpr size_t kPartOffset = kAmaxOffset + kAmaxBytes;
 
 struct WsLayout {

@@ -378,7 +378,8 @@ __device__ __forceinline__ void amax_fold16(const GemmArgs& a, bool live, int n,
             const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, off);
             k = o > k ? o : k;
         }
-        if ((threadIdx.x & 31) == 0 && k != 0ull) atomicMax(a.amax_keys + m + j, k);
+        if ((threadIdx.x & 31) == 0 && k != 0ull)
+            atomicMax(a.amax_keys + (size_t)(m + j) * (kAmaxKeyStride / 8), k);
     }
 }
 
@@ -787,7 +788,8 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             if (*last_flag) {
                 __threadfence();
                 for (int m = ep; m < a.M; m += kTcEpiThreads) {
-                    const unsigned long long k = atomicExch(a.amax_keys + m, 0ull);
+                    const unsigned long long k =
+                        atomicExch(a.amax_keys + (size_t)m * (kAmaxKeyStride / 8), 0ull);
                     a.amax_idx[m] = k ? (int64_t)(0xFFFFFFFFu - (uint32_t)k) : (int64_t)-1;
                     if (a.amax_best) a.amax_best[m] = amax_value(k);
                 }
