@@ -44,7 +44,9 @@ typedef struct nk_peer_group {
  * world ranks; 0 for arguments out of range. */
 NK_API size_t nk_peer_buffer_bytes(int max_elems, int world);
 
-/* cudaMalloc + zero of a receive buffer on the current device; nk_peer_free releases it. */
+/* cudaMalloc + zero of a receive buffer on the current device, rounded up to whole 2 MiB so it
+ * is a memory block of its own (CUDA IPC shares the underlying block, which for small
+ * allocations may hold other allocations too); nk_peer_free releases it. */
 NK_API int nk_peer_alloc(size_t bytes, void** ptr);
 NK_API int nk_peer_free(void* ptr);
 

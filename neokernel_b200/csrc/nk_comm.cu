@@ -113,9 +113,16 @@ extern "C" size_t nk_peer_buffer_bytes(int max_elems, int world) {
     return kArHeader + 2ull * (size_t)world * (size_t)max_elems * sizeof(float);
 }
 
+// CUDA IPC shares the driver's underlying memory block, and small cudaMalloc allocations may
+// be placed together in one block, so exporting one can expose its neighbours to the peer
+// processes. Every peer buffer is rounded up to whole 2 MiB (the size CUDA's documentation
+// recommends for shared allocations), so it is a block of its own and exposes nothing else.
+constexpr size_t kIpcGranule = 2u << 20;
+
 extern "C" int nk_peer_alloc(size_t bytes, void** ptr) {
     if (!ptr || bytes == 0) return NK_ERR_ARG;
     *ptr = nullptr;
+    bytes = (bytes + kIpcGranule - 1) / kIpcGranule * kIpcGranule;
     if (cudaMalloc(ptr, bytes) != cudaSuccess) return NK_ERR_CUDA;
     if (cudaMemset(*ptr, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
         cudaFree(*ptr);
