@@ -1,7 +1,8 @@
 /*
  * nk_gemm.h — C ABI of the B200 (sm_100a) decode-GEMM library `libnkgemm.so`.
  *
- * One operation is exported: the bf16 decode linear
+ * The operation exported here is the bf16 decode linear (with its greedy-head form, which
+ * also returns each row's argmax, and its fp32-output and workspace-free forms)
  *
  *     y[M, N] = bf16_rne( sum_k  f32(x[M, k]) * f32(W[N, k]) )      (fp32 accumulation)
  *

@@ -86,7 +86,7 @@ def test_qwen3_8b_128_greedy_tokens(batch):
         return [int(eq[i].logical_not().nonzero()[0]) if not eq[i].all() else None
                 for i in range(a.shape[0])]
 
-    # Teacher-forced replay of our tokens on the reference path (the judge's check).
+    # Teacher-forced replay of our tokens on the reference path (neokernel/judge.py:89-107).
     ref_logits = ref.teacher_forced_logits(prompt, t_ours)
     m = margins(ref_logits, t_ours)
     first_diff = first_divergence(t_ours, t_ref)
