@@ -267,3 +267,14 @@ def test_argmax_entry_rejects_before_launch():
     # no logits: y may be NULL, but nk_gemm_bf16 itself still needs y
     assert am(p, y=None, ws=0x100010) == _lib.NK_ERR_ALIGN
     assert call(p, y=0) == _lib.NK_ERR_ARG
+
+
+def test_python_greedy_head_rejects_bad_arguments():
+    import torch
+    a = torch.zeros(2, 8, dtype=torch.bfloat16)
+    w = torch.zeros(4, 8, dtype=torch.bfloat16)
+    idx = torch.empty(2, dtype=torch.int64)
+    with pytest.raises(ValueError, match="CUDA"):
+        nk.mm_argmax(a, w.t(), idx=idx)
+    with pytest.raises(ValueError, match="bfloat16"):
+        nk.mm_argmax(a.float(), w.t(), idx=idx)
