@@ -278,3 +278,36 @@ def test_python_greedy_head_rejects_bad_arguments():
         nk.mm_argmax(a, w.t(), idx=idx)
     with pytest.raises(ValueError, match="bfloat16"):
         nk.mm_argmax(a.float(), w.t(), idx=idx)
+
+
+def _amax_key(h, n):
+    """The greedy head's key (nk_tc.cu amax_key) for bf16 bits h at vocabulary index n."""
+    h = 0 if h == 0x8000 else h
+    if (h & 0x7FFF) > 0x7F80:
+        o = 0xFFFF
+    elif h & 0x8000:
+        o = ~h & 0xFFFF
+    else:
+        o = h | 0x8000
+    return (o << 32) | (0xFFFFFFFF - n)
+
+
+def test_greedy_head_key_order_is_torch_argmax_order():
+    """The largest key is torch.argmax's choice over the same bf16 row: the largest value, the
+    lowest index among equal values, -0 equal to +0, a NaN above everything (first NaN)."""
+    import torch
+    g = torch.Generator().manual_seed(5)
+    specials = torch.tensor([0.0, -0.0, float("inf"), -float("inf"), 1e-40, -1e-40, 3.0, -3.0],
+                            dtype=torch.bfloat16)
+    for trial in range(300):
+        n = int(torch.randint(1, 64, (1,), generator=g))
+        row = (torch.randn(n, generator=g) * 4).round().to(torch.bfloat16)  # many ties
+        if trial % 3 == 0:
+            k = int(torch.randint(0, n, (1,), generator=g))
+            row[k] = specials[trial % len(specials)]
+        if trial % 50 == 7:
+            row[n // 2] = float("nan")
+        bits = row.view(torch.int16).to(torch.int32) & 0xFFFF
+        keys = [_amax_key(int(b), i) for i, b in enumerate(bits)]
+        best = max(range(n), key=lambda i: keys[i])
+        assert best == int(torch.argmax(row.float())), (trial, row.tolist())
