@@ -144,9 +144,12 @@ NK_API int nk_gemm_bf16(const void* x, int64_t ldx,
  * (else NK_ERR_PLAN); a plan whose nk_ws_bytes() exceeds the array is refused with
  * NK_ERR_WORKSPACE. Nothing is allocated. The first call on each device (with that device
  * current) looks up the array's device address, so make it before any stream capture on that
- * device. All calls on a device share the array and it keeps the last call's contents: each
- * call clears the region it uses first, and calls that overlap on the GPU race — order them
- * (one stream, or streams joined by events).
+ * device; the address is kept for the life of the process (a cudaDeviceReset that unloads the
+ * library is not supported here). `stream` must belong to the current device (else
+ * NK_ERR_DEVICE). All calls on a device share the array and it keeps the last call's
+ * contents: each call first clears the tickets and partial slots its plan uses, and calls that
+ * overlap on the GPU race — order them (one stream, or streams joined by events). A call
+ * refused for its arguments writes nothing.
  */
 #define NK_STATIC_SCRATCH_BYTES (8u << 20)
 NK_API int nk_gemm_bf16_static(const void* x, int64_t ldx,
@@ -196,6 +199,16 @@ NK_API int nk_gemm_bf16_argmax(const void* x, int64_t ldx,
 /* Read and clear the device error word that bounded waits set on timeout (synchronizes
  * `stream`). Writes NK_OK or NK_ERR_TIMEOUT to *status. */
 NK_API int nk_device_error(nk_stream_t stream, int* status);
+
+/* Failure-detection tests only; no counterpart in the reference (its torch.mm has no
+ * device-side wait). The next tensor-core launch (any entry point above) runs with the
+ * rank-1 CTA of output tile `tile` keeping its fp32 partial to itself, so the CTA that
+ * finishes that tile waits for it until its bounded wait expires (about 2 s): the tile's
+ * outputs are not written, the launch returns, nk_device_error then reports NK_ERR_TIMEOUT,
+ * and the workspace needs nk_ws_init before its next use. The request is consumed by that
+ * one launch (a tile with a single CTA, a forced split_k grid larger than one resident wave,
+ * or -1 withhold nothing). Nothing faults or hangs. */
+NK_API int nk_test_withhold_partial(int tile);
 
 /* Human-readable text for a status code (static storage). */
 NK_API const char* nk_status_string(int status);

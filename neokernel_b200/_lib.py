@@ -40,7 +40,7 @@ EXPORTS = ("nk_plan_make", "nk_ws_bytes", "nk_ws_init", "nk_gemm_bf16", "nk_devi
            "nk_rmsnorm_bf16", "nk_qk_norm_rope_cache_bf16", "nk_attention_ws_bytes",
            "nk_attention_decode_bf16", "nk_silu_mul_bf16", "nk_peer_buffer_bytes", "nk_peer_alloc",
            "nk_peer_free", "nk_ipc_handle", "nk_ipc_open", "nk_ipc_close", "nk_allreduce_bf16",
-           "nk_gemm_argmax_ws_bytes", "nk_gemm_bf16_argmax")
+           "nk_gemm_argmax_ws_bytes", "nk_gemm_bf16_argmax", "nk_test_withhold_partial")
 
 
 NK_PEER_MAX_RANKS = 8
@@ -147,6 +147,8 @@ def load() -> ctypes.CDLL:
     L.nk_ipc_close.restype = i32
     L.nk_allreduce_bf16.argtypes = [vp, vp, i32, ctypes.POINTER(NkPeerGroup), vp]
     L.nk_allreduce_bf16.restype = i32
+    L.nk_test_withhold_partial.argtypes = [i32]
+    L.nk_test_withhold_partial.restype = i32
     L.nk_device_error.argtypes = [vp, ctypes.POINTER(i32)]
     L.nk_device_error.restype = i32
     L.nk_status_string.argtypes = [i32]

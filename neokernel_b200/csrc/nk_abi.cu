@@ -7,9 +7,15 @@
 // configuration before launching anything; it never allocates and never synchronizes.
 #include <string.h>
 
+#include <atomic>
+
 #include "nk_common.cuh"
 
 namespace nk {
+
+// Output tile whose rank-1 partial the next tensor-core launch withholds (-1 = none); set by
+// nk_test_withhold_partial and consumed by that launch.
+static std::atomic<int> g_withhold_tile{-1};
 
 // Per-device "is this an sm_100 part" cache (checked once per device, then free).
 static int g_device_ok[64];  // 0 = unknown, 1 = ok, -1 = not sm_100
@@ -166,6 +172,12 @@ struct AmaxOut {
     void* best;
 };
 
+// Every check of a linear's arguments that involves neither the workspace nor the device
+// (plan, shape, pointers, alignment). Returns NK_OK or the NK_ERR_* the entry point reports.
+static int gemm_validate(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* y,
+                         int64_t ldy, bool y_f32, int M, int N, int K, const nk_plan* p,
+                         const AmaxOut* amax);
+
 // Shared body of nk_gemm_bf16 (bf16 y), nk_gemm_bf16_f32out (fp32 y) and
 // nk_gemm_bf16_argmax (bf16 y or none, plus the per-token argmax).
 static int gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
@@ -186,9 +198,9 @@ extern "C" int nk_gemm_bf16_f32out(const void* x, int64_t ldx, const void* w, in
     return gemm_impl(x, ldx, w, ldw, y, ldy, true, M, N, K, p, ws, ws_bytes, stream);
 }
 
-static int nk::gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
-                         int64_t ldy, bool y_f32, int M, int N, int K, const nk_plan* p,
-                         void* ws, size_t ws_bytes, nk_stream_t stream, const AmaxOut* amax) {
+static int nk::gemm_validate(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                             const void* y, int64_t ldy, bool y_f32, int M, int N, int K,
+                             const nk_plan* p, const AmaxOut* amax) {
     if (!p || p->magic != NK_PLAN_MAGIC) return NK_ERR_PLAN;
     if (p->N != N || p->K != K) return NK_ERR_PLAN;
     if (M < 1 || M > p->M_max) return NK_ERR_SHAPE;
@@ -199,14 +211,24 @@ static int nk::gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw,
         if (!amax->idx) return NK_ERR_ARG;
         if (((uintptr_t)amax->idx & 7u) || ((uintptr_t)amax->best & 1u)) return NK_ERR_ALIGN;
         if (p->M_max > kAmaxMaxTokens) return NK_ERR_SHAPE;
-        if (!ws || ws_bytes < amax_ws_bytes(*p)) return NK_ERR_WORKSPACE;
-        if (((uintptr_t)ws & 255u) != 0) return NK_ERR_ALIGN;
     }
     if (!aligned2(x) || !aligned2(w) || !aligned2(y)) return NK_ERR_ALIGN;
     if (y_f32 && ((uintptr_t)y & 3u) != 0) return NK_ERR_ALIGN;
     if (p->kind == NK_KIND_GEMV || p->kind == NK_KIND_TC) {
         if (!aligned16(x) || !aligned16(w) || (ldx % 8) != 0 || (ldw % 8) != 0)
             return NK_ERR_ALIGN;
+    }
+    return NK_OK;
+}
+
+static int nk::gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
+                         int64_t ldy, bool y_f32, int M, int N, int K, const nk_plan* p,
+                         void* ws, size_t ws_bytes, nk_stream_t stream, const AmaxOut* amax) {
+    const int valid = gemm_validate(x, ldx, w, ldw, y, ldy, y_f32, M, N, K, p, amax);
+    if (valid != NK_OK) return valid;
+    if (amax) {
+        if (!ws || ws_bytes < amax_ws_bytes(*p)) return NK_ERR_WORKSPACE;
+        if (((uintptr_t)ws & 255u) != 0) return NK_ERR_ALIGN;
     }
     const WsLayout L = ws_layout(*p);
     if (L.total > 0) {
@@ -229,6 +251,7 @@ static int nk::gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw,
     a.amax_done = nullptr;
     a.amax_idx = nullptr;
     a.amax_best = nullptr;
+    a.withhold_tile = p->kind == NK_KIND_TC ? g_withhold_tile.exchange(-1) : -1;
     if (amax) {
         a.amax_keys =  // keys kAmaxKeyStride bytes apart
             reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + kAmaxOffset);
@@ -258,6 +281,12 @@ extern "C" int nk_gemm_bf16_argmax(const void* x, int64_t ldx, const void* w, in
                                    nk_stream_t stream) {
     const AmaxOut out{idx, best};
     return gemm_impl(x, ldx, w, ldw, y, ldy, false, M, N, K, p, ws, ws_bytes, stream, &out);
+}
+
+extern "C" int nk_test_withhold_partial(int tile) {
+    if (tile < -1) return NK_ERR_ARG;
+    g_withhold_tile.store(tile);
+    return NK_OK;
 }
 
 extern "C" int nk_device_error(nk_stream_t stream, int* status) {

@@ -240,6 +240,8 @@ struct GemmArgs {
     int segments;           // partial slots per tile
     int part_cols;          // token columns per partial slot (min(NT, M_max))
     int coresident;         // 1: every CTA of the grid is resident at once (see nk_tc.cu)
+    int withhold_tile;      // failure-detection tests only (nk_test_withhold_partial): the
+                            // rank-1 CTA of this output tile publishes no partial; -1 = none
     TcPartition part_map;
     // greedy head (nk_gemm_bf16_argmax) only; all nullptr otherwise
     unsigned long long* amax_keys;  // [M] (ordered value, inverted index) keys, zero between calls

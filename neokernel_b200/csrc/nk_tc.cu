@@ -582,6 +582,9 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             uint64_t* const slot0 = reinterpret_cast<uint64_t*>(a.part) + row0;
             float* const part0 = a.part + row0;
             const bool finisher = !whole && rank == 0 && wait_mode;
+            // Failure-detection tests only: this CTA keeps its partial to itself, so the tile's
+            // finisher's bounded wait runs out (NK_ERR_TIMEOUT) instead of completing.
+            const bool withhold = wait_mode && rank == 1 && sg.t == a.withhold_tile;
             // Rank 0 of a shared tile holds the tile's first K blocks as its last segment; the
             // other ranks (higher CTAs) hold the rest. It waits for them while its own last
             // MMAs still run and, for the decode token tile, already adds up their partials
@@ -633,7 +636,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                 // Publish this rank's fp32 partial: as tagged slots (a value and its tag in one
                 // 64-bit store, so no fence or count follows), or as plain fp32 followed below
                 // by a fence and the tile's count.
-                if (ok) {
+                if (ok && !withhold) {
 #pragma unroll 1
                     for (int c0 = 0; c0 < NT; c0 += 16) {
                         if (c0 >= mcount) break;  // warp-uniform
@@ -741,7 +744,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             if (!whole && wait_mode && !tagged && rank > 0) {
                 __threadfence();  // this CTA's partial stores, before the count that publishes them
                 epi_bar();
-                if (ep == 0) atomicAdd(a.tickets + sg.t, 1u);
+                if (ep == 0 && !withhold) atomicAdd(a.tickets + sg.t, 1u);
             } else if (!whole && !wait_mode) {
                 // Without a co-resident grid every rank publishes plain partials (rank 0 above as
                 // well) and the CTA whose arrival completes the tile's count sums them, in the

@@ -74,6 +74,9 @@ class Plan:
 
 _PLANS: dict = {}
 _WORKSPACES: dict = {}
+# Workspaces replaced by a larger one. They are never freed: a CUDA graph captured while one
+# of them was current still writes split-K tickets and partials into it on every replay.
+_RETIRED: list = []
 
 
 def plan_for(M: int, N: int, K: int, kind: int = KIND_AUTO, split_k: int = 0) -> Plan:
@@ -94,6 +97,13 @@ def workspace(nbytes: int, device: torch.device, stream: torch.cuda.Stream) -> t
     stream is not being captured — run one eager call of each shape before capturing a CUDA
     graph, as the reference engine does with its three warm-up decodes
     (engine/engine.py:119-125).
+
+    A workspace that must grow is replaced, never freed: the old one stays allocated for the
+    life of the process, because a graph captured while it was current keeps using it on
+    every replay (and torch reuses stream handles, so two decoders may share a key). Sizes
+    grow at least twofold, so the retired buffers total less than the current one. The new
+    buffer is allocated on ``stream`` itself, so the caching allocator never hands it out
+    while work of another stream may still use that memory.
     """
     key = (device.index, stream.cuda_stream)
     ws = _WORKSPACES.get(key)
@@ -101,13 +111,16 @@ def workspace(nbytes: int, device: torch.device, stream: torch.cuda.Stream) -> t
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError("neokernel_b200: split-K workspace must be sized before CUDA "
                                "graph capture; run the call once eagerly first")
-        size = max(nbytes, 1 << 20)
+        size = max(nbytes, 1 << 20, 2 * ws.numel() if ws is not None else 0)
         size = (size + (1 << 20) - 1) >> 20 << 20
-        ws = torch.empty(size, dtype=torch.uint8, device=device)
-        status = _lib.load().nk_ws_init(ws.data_ptr(), size, stream.cuda_stream)
+        with torch.cuda.device(device), torch.cuda.stream(stream):
+            new = torch.empty(size, dtype=torch.uint8, device=device)
+        status = _lib.load().nk_ws_init(new.data_ptr(), size, stream.cuda_stream)
         if status != _lib.NK_OK:
             _raise(status, "nk_ws_init")
-        _WORKSPACES[key] = ws
+        if ws is not None:
+            _RETIRED.append(ws)
+        _WORKSPACES[key] = ws = new
     return ws
 
 
@@ -192,6 +205,15 @@ def _mm(a, b, out, plan, stream, f32):
     return out
 
 
+def _rows_vector(t: torch.Tensor, M: int) -> bool:
+    """``t`` holds one element per row, M elements adjacent in memory: [M] or [M, 1]."""
+    if t.dim() == 2 and t.shape[1] != 1:
+        return False
+    if t.dim() not in (1, 2) or t.shape[0] != M:
+        return False
+    return M <= 1 or t.stride(0) == 1
+
+
 def mm_argmax(a: torch.Tensor, b: torch.Tensor, *, idx: torch.Tensor,
               logits: torch.Tensor | None = None, best: torch.Tensor | None = None,
               plan: Plan | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
@@ -200,9 +222,10 @@ def mm_argmax(a: torch.Tensor, b: torch.Tensor, *, idx: torch.Tensor,
     engine/engine.py:114-116 in one launch, the argmax folded into the linear's epilogue.
 
     a: bf16 CUDA [M, K]; b = W.t() of a row-major [N, K] weight (as ``mm``); idx: int64 CUDA
-    [M]. ``logits`` (bf16 [M, N], unit column stride) is written only if given, so the
-    [M, N] logits need not be stored; ``best`` (bf16 [M]) receives each row's maximum.
-    Tensor-core plans only (16-byte aligned operands, K a multiple of 8).
+    [M] or [M, 1] — the engine's ``next_tokens`` is [B, 1] (``keepdim=True``,
+    engine/engine.py:91,116). ``logits`` (bf16 [M, N], unit column stride) is written only if
+    given, so the [M, N] logits need not be stored; ``best`` (bf16 [M] or [M, 1]) receives
+    each row's maximum. Tensor-core plans only (16-byte aligned operands, K a multiple of 8).
     """
     _check_tensor(a, "a")
     _check_tensor(b, "b")
@@ -212,16 +235,16 @@ def mm_argmax(a: torch.Tensor, b: torch.Tensor, *, idx: torch.Tensor,
         raise ValueError(f"mm_argmax: a is [{M}, {K}] but b is [{K2}, {N}]")
     if not isinstance(idx, torch.Tensor) or idx.dtype != torch.int64 or idx.device != a.device:
         raise ValueError("mm_argmax: idx must be an int64 tensor on a's device")
-    if idx.dim() != 1 or idx.shape[0] != M or (M > 1 and idx.stride(0) != 1):
-        raise ValueError(f"mm_argmax: idx must be a contiguous [{M}] tensor")
+    if not _rows_vector(idx, M):
+        raise ValueError(f"mm_argmax: idx must be a contiguous [{M}] or [{M}, 1] tensor")
     if logits is not None:
         _check_tensor(logits, "logits")
         if tuple(logits.shape) != (M, N) or (N > 1 and logits.stride(1) != 1):
             raise ValueError(f"mm_argmax: logits must be [{M}, {N}] with unit stride along N")
     if best is not None:
-        if (best.dtype != torch.bfloat16 or best.device != a.device or best.dim() != 1
-                or best.shape[0] != M or (M > 1 and best.stride(0) != 1)):
-            raise ValueError(f"mm_argmax: best must be a contiguous bf16 [{M}] tensor")
+        if best.dtype != torch.bfloat16 or best.device != a.device or not _rows_vector(best, M):
+            raise ValueError(f"mm_argmax: best must be a contiguous bf16 [{M}] or [{M}, 1] "
+                             "tensor")
     if b.device != a.device:
         raise ValueError("mm_argmax: a and b must be on the same device")
     if M == 0:

@@ -21,8 +21,21 @@ engine/kernels/elementwise.py:81-88). Every buffer is allocated once in ``prepar
 position lives on the device, so a step can be captured in one CUDA graph and replayed (the
 reference captures its decode the same way, engine/engine.py:119-129).
 
-Weights are random (seeded, ``normal_(0, 0.02)`` for matrices, ones for norm gains as in the
-reference kernel test, tests/test_hand_rolled_kernels.py:154-156); no checkpoint is used.
+Weights are random and seeded; no checkpoint is used. Two initialisations (``init``):
+
+* ``"decisive"`` (default): every greedy choice is made by a wide margin, so two correct
+  implementations of the step emit the same tokens. The embedding is N(0, 1), so the residual
+  stream is led by the current token; QKV and gate_up are N(0, 0.02); the residual projections
+  o_proj and down are N(0, 0.02 / sqrt(2 * layers)) (the scaled residual init of GPT-2-style
+  models), so the 2 * layers branch outputs add up to about the embedding's size; the
+  lm_head's row v is the embedding row of token perm(v) scaled by 1 / sqrt(hidden), for a
+  seeded random permutation ``perm``, so the token after t is most often perm^-1(t) with
+  a logit near 1 * sqrt(hidden) * gain, tens of logits above the rest; every norm gain is
+  drawn from U(0.5, 1.5), so no multiplication by a gain is the identity.
+* ``"reference"``: the reference kernel test's init (tests/test_hand_rolled_kernels.py:
+  154-156): ``normal_(0, 0.02)`` for every matrix and ones for the norm gains. Its logits are
+  nearly flat (top-2 gaps of a few hundredths), so greedy tokens flip on genuine near-ties
+  between any two valid fp32-accumulating GEMMs.
 """
 
 from __future__ import annotations
@@ -65,42 +78,79 @@ QWEN3_8B = Qwen3Dims(4096, 12288, 32, 8, 128, 36, 151936)
 QWEN3_32B = Qwen3Dims(5120, 25600, 64, 8, 128, 64, 151936)
 
 
+INITS = ("decisive", "reference")
+
+
 def _randn(shape, gen, device, std=0.02):
     t = torch.randn(shape, generator=gen, device=device, dtype=torch.float32)
     return t.mul_(std).to(torch.bfloat16)
 
 
+def _gain(n, gen, device, init):
+    """A norm gain: ones (reference init) or U(0.5, 1.5) (decisive init)."""
+    if init == "reference":
+        return torch.ones(n, device=device, dtype=torch.bfloat16)
+    t = torch.rand(n, generator=gen, device=device, dtype=torch.float32)
+    return t.add_(0.5).to(torch.bfloat16)
+
+
+def _check_init(init):
+    if init not in INITS:
+        raise ValueError(f"init must be one of {INITS}, not {init!r}")
+
+
 class LayerWeights:
     """One layer's weights in the reference's packed layout (engine/kernels/weights.py:10-25):
     row-major ``qkv_weight [Nq+2Nkv, H]`` and ``gate_up_weight [2I, H]``; the linears take
-    their ``.t()`` views."""
+    their ``.t()`` views. Drawn in a fixed order from ``gen``."""
 
-    def __init__(self, d: Qwen3Dims, gen, device):
+    def __init__(self, d: Qwen3Dims, gen, device, init: str = "decisive"):
+        _check_init(init)
         H, I = d.hidden, d.intermediate
+        res_std = 0.02 if init == "reference" else 0.02 / math.sqrt(2 * d.layers)
         self.qkv_weight = _randn((d.qkv_width, H), gen, device)
-        self.o_weight = _randn((H, d.q_width), gen, device)
+        self.o_weight = _randn((H, d.q_width), gen, device, res_std)
         self.gate_up_weight = _randn((2 * I, H), gen, device)
-        self.down_weight = _randn((H, I), gen, device)
+        self.down_weight = _randn((H, I), gen, device, res_std)
         self.qkv = self.qkv_weight.t()
         self.o = self.o_weight.t()
         self.gate_up = self.gate_up_weight.t()
         self.down = self.down_weight.t()
-        ones = lambda n: torch.ones(n, device=device, dtype=torch.bfloat16)  # noqa: E731
-        self.input_norm = ones(H)
-        self.post_norm = ones(H)
-        self.q_norm = ones(d.head_dim)
-        self.k_norm = ones(d.head_dim)
+        self.input_norm = _gain(H, gen, device, init)
+        self.post_norm = _gain(H, gen, device, init)
+        self.q_norm = _gain(d.head_dim, gen, device, init)
+        self.k_norm = _gain(d.head_dim, gen, device, init)
+
+
+def draw_embedding(d: Qwen3Dims, gen, device, init: str):
+    """The token embedding [vocab, hidden]: the first draw of a model."""
+    return _randn((d.vocab, d.hidden), gen, device, 0.02 if init == "reference" else 1.0)
+
+
+def draw_head(d: Qwen3Dims, embed, gen, device, init: str):
+    """(final-norm gain, lm_head weight [vocab, hidden]): the last draws of a model. Tied
+    models use the embedding itself; an untied decisive model the permuted, scaled embedding
+    rows (row v = embed[perm[v]] / sqrt(hidden))."""
+    final_norm = _gain(d.hidden, gen, device, init)
+    if d.tie_embeddings:
+        return final_norm, embed
+    if init == "reference":
+        return final_norm, _randn((d.vocab, d.hidden), gen, device)
+    perm = torch.randperm(d.vocab, generator=gen, device=device)
+    head = (embed.index_select(0, perm).float() * (1.0 / math.sqrt(d.hidden))).to(torch.bfloat16)
+    return final_norm, head
 
 
 class Qwen3Weights:
-    def __init__(self, d: Qwen3Dims, seed: int = 0, device="cuda", layers: int | None = None):
-        self.dims = d
+    def __init__(self, d: Qwen3Dims, seed: int = 0, device="cuda", layers: int | None = None,
+                 init: str = "decisive"):
+        _check_init(init)
+        self.dims, self.init = d, init
         gen = torch.Generator(device=device).manual_seed(seed)
-        self.embed = _randn((d.vocab, d.hidden), gen, device)
+        self.embed = draw_embedding(d, gen, device, init)
         n = d.layers if layers is None else layers
-        self.layers = [LayerWeights(d, gen, device) for _ in range(n)]
-        self.final_norm = torch.ones(d.hidden, device=device, dtype=torch.bfloat16)
-        self.lm_head_weight = self.embed if d.tie_embeddings else _randn((d.vocab, d.hidden), gen, device)
+        self.layers = [LayerWeights(d, gen, device, init) for _ in range(n)]
+        self.final_norm, self.lm_head_weight = draw_head(d, self.embed, gen, device, init)
         self.lm_head = self.lm_head_weight.t()  # engine/engine.py:70
 
 

@@ -77,20 +77,19 @@ class TPWeights:
     never holds more than one full layer), sliced, and the full copy released."""
 
     def __init__(self, d: Qwen3Dims, seed: int, rank: int, world: int, device="cuda",
-                 layers: int | None = None):
+                 layers: int | None = None, init: str = "decisive"):
         self.full_dims = d
         self.dims = local_dims(d, world)
-        self.rank, self.world = rank, world
+        self.rank, self.world, self.init = rank, world, init
         gen = torch.Generator(device=device).manual_seed(seed)
-        self.embed = qwen3._randn((d.vocab, d.hidden), gen, device)
+        self.embed = qwen3.draw_embedding(d, gen, device, init)
         n = d.layers if layers is None else layers
         self.layers = []
         for _ in range(n):
-            full = qwen3.LayerWeights(d, gen, device)
+            full = qwen3.LayerWeights(d, gen, device, init)
             self.layers.append(TPLayerWeights(full, d, rank, world))
             del full
-        self.final_norm = torch.ones(d.hidden, device=device, dtype=torch.bfloat16)
-        head = self.embed if d.tie_embeddings else qwen3._randn((d.vocab, d.hidden), gen, device)
+        self.final_norm, head = qwen3.draw_head(d, self.embed, gen, device, init)
         vl = d.vocab // world
         self.lm_head_weight = head[rank * vl:(rank + 1) * vl].contiguous()
         self.lm_head = self.lm_head_weight.t()

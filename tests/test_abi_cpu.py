@@ -311,3 +311,35 @@ def test_greedy_head_key_order_is_torch_argmax_order():
         keys = [_amax_key(int(b), i) for i, b in enumerate(bits)]
         best = max(range(n), key=lambda i: keys[i])
         assert best == int(torch.argmax(row.float())), (trial, row.tolist())
+
+
+def test_static_entry_rejects_before_touching_its_scratch():
+    """nk_gemm_bf16_static checks every argument before it clears or uses the library's
+    scratch array, so a refused call reaches neither the device nor the array."""
+    L = _lib.load()
+    f = L.nk_gemm_bf16_static
+    vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    f.argtypes = [vp, i64, vp, i64, vp, i64, i32, i32, i32, ctypes.POINTER(_lib.NkPlan), vp]
+    f.restype = i32
+    st, p = make(4, 4096, 4096, 0, _lib.KIND_TC)
+    assert st == 0 and L.nk_ws_bytes(ctypes.byref(p)) > 0
+
+    def sc(plan=p, x=0x10000, ldx=4096, w=0x20000, ldw=4096, y=0x30000, ldy=4096, M=4):
+        return f(x, ldx, w, ldw, y, ldy, M, 4096, 4096,
+                 ctypes.byref(plan) if plan is not None else None, None)
+
+    assert sc(plan=None) == _lib.NK_ERR_PLAN
+    assert sc(M=5) == _lib.NK_ERR_SHAPE
+    assert sc(x=0) == _lib.NK_ERR_ARG
+    assert sc(x=0x10008) == _lib.NK_ERR_ALIGN
+    assert sc(ldw=4100) == _lib.NK_ERR_ALIGN
+    assert sc(y=0x30001) == _lib.NK_ERR_ALIGN
+    assert sc(ldy=100) == _lib.NK_ERR_SHAPE
+    # with valid arguments the next check is the device (there is none here)
+    assert sc() in (_lib.NK_ERR_CUDA, _lib.NK_ERR_DEVICE)
+
+
+def test_withhold_request_rejects_bad_tile():
+    L = _lib.load()
+    assert L.nk_test_withhold_partial(-5) == _lib.NK_ERR_ARG
+    assert L.nk_test_withhold_partial(-1) == 0

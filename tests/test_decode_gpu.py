@@ -1,13 +1,19 @@
 """Decode-step parity: the Qwen3 decode graph with the decode linears on neokernel_b200.mm
 against the same graph on torch.mm (the reference's own call, engine/kernels/decode.py:54-66,
-engine/engine.py:114), random-init weights, CUDA-graph replay.
+engine/engine.py:114), random-init weights, CUDA-graph replay. The torch.mm graph with PyTorch
+ops (qwen3.layer_step) is pinned to transformers' Qwen3 modules on the CPU
+(tests/test_step_model_cpu.py).
 
-Greedy tokens are compared over 128 generated tokens. Random-init models have near-flat
-logits (top-2 gaps of a few hundredths among 151,936 entries), so a flip is legitimate only
-where the reference's own logits were within rounding of a tie: every step where the tokens
-differ must pass the reference judge's margin rule (neokernel/judge.py:71-86) — the token we
-chose scores within 2.0 of the maximum of the torch.mm path's teacher-forced logits — and in
-practice within a few bf16 ulps. Identical-token counts are printed.
+With the decisive random init (qwen3.py) every greedy choice is made by a wide margin, and
+the north-star criterion holds as stated: identical greedy tokens over a 128-token decode, for
+the linears alone and for the whole product step (fused kernels, fused greedy head).
+
+With the reference test's init (N(0, 0.02) everywhere, unit gains) the logits are nearly flat
+(top-2 gaps of a few hundredths among 151,936 entries), so a flip is legitimate where the
+reference's own logits were within rounding of a tie: every step where the tokens differ must
+pass the reference judge's margin rule (neokernel/judge.py:71-86) — the token we chose scores
+within 2.0 of the maximum of the torch.mm path's teacher-forced logits — and in practice within
+a few bf16 ulps. Identical-token counts are printed.
 """
 
 import json
@@ -61,9 +67,49 @@ def test_two_layer_step_matches_torch_mm():
 
 
 @pytest.mark.parametrize("batch", (1, 4))
-def test_qwen3_8b_128_greedy_tokens(batch):
+def test_qwen3_8b_128_identical_greedy_tokens(batch):
+    """Decisive init: 128 identical greedy tokens per sequence on the reference's step (torch.mm,
+    PyTorch ops), on it with neokernel_b200.mm as the five linears, and on the product step
+    (fused decode kernels, neokernel_b200.mm, fused greedy head)."""
     d = qwen3.QWEN3_8B
-    w = qwen3.Qwen3Weights(d, seed=11)
+    w = qwen3.Qwen3Weights(d, seed=11, init="decisive")
+    prompt_len, new = 8, 128
+    cap = prompt_len + new
+    gen = torch.Generator(device="cuda").manual_seed(20260922)
+    prompt = torch.randint(0, d.vocab, (batch, prompt_len), generator=gen, device="cuda")
+    ref = qwen3.GraphDecoder(w, batch, cap, torch.mm)
+    t_ref = ref.greedy(prompt, new)
+    lr = ref.teacher_forced_logits(prompt, t_ref)
+    top2 = lr.topk(2, dim=-1).values
+    gap = (top2[..., 0] - top2[..., 1]).flatten()
+    report = {"test": f"qwen3-8b/decisive/B{batch}", "tokens": batch * new,
+              "distinct_tokens": int(t_ref.unique().numel()),
+              "top2_margin": {"min": float(gap.min()), "p1": float(gap.quantile(0.01)),
+                              "median": float(gap.median()), "max": float(gap.max())}}
+    ours = qwen3.GraphDecoder(w, batch, cap, nk.mm)
+    t_ours = ours.greedy(prompt, new)
+    lo = ours.teacher_forced_logits(prompt, t_ref)
+    report["linears_identical_tokens"] = int((t_ours == t_ref).sum())
+    report["linears_teacher_forced_max_logit_diff"] = float((lo - lr).abs().max())
+    del ours
+    prod = qwen3.GraphDecoder(w, batch, cap, nk.mm, fused=True, fused_head=True)
+    t_prod = prod.greedy(prompt, new)
+    report["product_identical_tokens"] = int((t_prod == t_ref).sum())
+    print(json.dumps(report), flush=True)
+    assert torch.equal(t_ours, t_ref), report
+    assert torch.equal(t_prod, t_ref), report
+    assert report["distinct_tokens"] > new // 2, report  # a walk through the vocabulary
+    # the margins the init is chosen for: far above the logit noise of either path
+    assert report["top2_margin"]["min"] > 8 * max(report["linears_teacher_forced_max_logit_diff"],
+                                                  0.125), report
+    del ref, prod
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("batch", (1, 4))
+def test_qwen3_8b_reference_init_flips_only_at_near_ties(batch):
+    d = qwen3.QWEN3_8B
+    w = qwen3.Qwen3Weights(d, seed=11, init="reference")
     prompt_len, new = 8, 128
     cap = prompt_len + new
     gen = torch.Generator(device="cuda").manual_seed(20260922)
@@ -97,7 +143,7 @@ def test_qwen3_8b_128_greedy_tokens(batch):
     lc = ctrl.teacher_forced_logits(prompt, t_ref)
     agree = (lo.argmax(-1) == lr.argmax(-1)).float().mean().item()
     agree_ctrl = (lc.argmax(-1) == lr.argmax(-1)).float().mean().item()
-    report = {"test": f"qwen3-8b/greedy/B{batch}", "identical_tokens": int(same.sum()),
+    report = {"test": f"qwen3-8b/reference-init/B{batch}", "identical_tokens": int(same.sum()),
               "tokens": batch * new, "first_divergence": first_diff,
               "control_first_divergence": first_divergence(t_ctrl, t_ref),
               "teacher_forced_argmax_agreement": agree,

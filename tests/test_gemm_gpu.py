@@ -311,6 +311,56 @@ def test_cuda_graph_capture_and_replay():
         del graph
 
 
+def test_graph_survives_workspace_growth_on_its_stream():
+    """A graph captured on a stream keeps working when a later eager call on that stream needs
+    a larger split-K workspace: the old workspace is retired, never freed, so memory the graph
+    still writes to is not handed to another tensor."""
+    dev = torch.device(DEV, torch.cuda.current_device())
+    stream = torch.cuda.Stream()
+    N, K, M = 4096, 4096, 1
+    W = synthetic.weight(N, K, seed=61, device=DEV)
+    x = synthetic.activation(M, K, seed=62, device=DEV)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=DEV)
+    plan = nk.plan_for(M, N, K)
+    assert plan.ws_bytes > 0
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            nk.mm(x, W.t(), out=y, plan=plan)
+    stream.synchronize()
+    eager = y.clone()
+    before = nk.workspace(1, dev, stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        nk.mm(x, W.t(), out=y, plan=plan)
+    # Larger plans run eagerly on the same stream: the lm_head at 16 tokens and the greedy
+    # head grow the stream's workspace.
+    Nh = 151936
+    Wh = synthetic.weight(Nh, K, seed=63, device=DEV)
+    xh = synthetic.activation(16, K, seed=64, device=DEV)
+    yh = torch.empty((16, Nh), dtype=torch.bfloat16, device=DEV)
+    idx = torch.empty((16, 1), dtype=torch.int64, device=DEV)
+    with torch.cuda.stream(stream):
+        nk.mm(xh, Wh.t(), out=yh)
+        nk.mm_argmax(xh, Wh.t(), idx=idx)
+        after = nk.workspace(1, dev, stream)
+        assert after.data_ptr() != before.data_ptr() and after.numel() > before.numel()
+        # Whatever memory is free now is taken and filled with a pattern the kernels would
+        # misread as work in progress.
+        junk = [torch.full((before.numel(),), 0xFF, dtype=torch.uint8, device=DEV)
+                for _ in range(8)]
+    stream.synchronize()
+    assert torch.equal(idx[:, 0], yh.float().argmax(dim=-1))
+    for _ in range(3):
+        y.zero_()
+        torch.cuda.synchronize()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(y, eager)
+    assert nk.device_error() == 0
+    del graph, junk
+
+
 def test_shim_errors_on_gpu():
     W = synthetic.weight(64, 128, 1, device=DEV)
     x = synthetic.activation(2, 128, 2, device=DEV)

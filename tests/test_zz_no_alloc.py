@@ -95,3 +95,23 @@ def test_static_entry_point_refuses_oversized_or_foreign_plans():
     st = L.nk_gemm_bf16_static(dummy.data_ptr(), 4096, dummy.data_ptr(), 4096, dummy.data_ptr(),
                                4096, 1, 4096, 4096, ctypes.byref(gemv), stream)
     assert st == _lib.NK_ERR_PLAN
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_static_entry_point_refuses_a_stream_of_another_device():
+    """The scratch array is per device: a stream of device 1 while device 0 is current would
+    make the kernels use device 0's copy from device 1, so the call is refused untouched."""
+    L = bind()
+    M, N, K = 4, 4096, 4096
+    with torch.cuda.device(0):
+        plan = make_plan(L, M, N, K)
+        assert L.nk_ws_bytes(ctypes.byref(plan)) > 0
+        W = synthetic.weight(N, K, seed=1, device="cuda:0")
+        x = synthetic.activation(M, K, seed=2, device="cuda:0")
+        y = torch.zeros((M, N), dtype=torch.bfloat16, device="cuda:0")
+        other = torch.cuda.Stream(device=1)
+        st = L.nk_gemm_bf16_static(x.data_ptr(), K, W.data_ptr(), K, y.data_ptr(), N, M, N, K,
+                                   ctypes.byref(plan), other.cuda_stream)
+        assert st == _lib.NK_ERR_DEVICE
+        torch.cuda.synchronize()
+        assert not y.any()
