@@ -219,6 +219,32 @@ def cpu_reference(m_list, budget_s=10.0, warmup=1):
             "cpu": _cpu_model()}
 
 
+def cpu_config1(runs=200, warmup=20):
+    """The reference's CPU path on the single decode linear of its first benchmark case:
+    torch.mm(x, W.t()) with M=1, K=1024, N=3072 (the Qwen3-0.6B gate_proj shape), W bf16
+    ~N(0, 0.02), x bf16 ~N(0, 1), seed 0, fp32 accumulation, bf16 output; median of ``runs``
+    timed runs after ``warmup``, all host threads."""
+    from neokernel_b200 import synthetic
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    M, K, N = 1, 1024, 3072
+    W = synthetic.weight(N, K, seed=0)
+    x = synthetic.activation(M, K, seed=0)
+    y = torch.empty((M, N), dtype=torch.bfloat16)
+    for _ in range(warmup):
+        torch.mm(x, W.t(), out=y)
+    ts = []
+    for _ in range(runs):
+        t0 = time.perf_counter()
+        torch.mm(x, W.t(), out=y)
+        ts.append(time.perf_counter() - t0)
+    us = statistics.median(ts) * 1e6
+    err = float((y.float() - torch.matmul(x.float(), W.float().t())).abs().max())
+    return {"shape": "M=1 K=1024 N=3072", "runs": runs, "median_us": round(us, 2),
+            "GB/s": round(gemm_bytes(M, N, K) / (us * 1e-6) / 1e9, 2), "threads": threads,
+            "cpu": _cpu_model(), "max_abs_err_vs_fp32": err, "tolerance": 2e-2}
+
+
 def _cpu_model():
     try:
         for line in open("/proc/cpuinfo"):
@@ -301,15 +327,21 @@ def main():
     ap.add_argument("--no-decode", action="store_true",
                     help="skip the 36-layer Qwen3-8B decode-step tok/s measurement")
     ap.add_argument("--decode-batches", default="1,16")
-    ap.add_argument("--tp-decode", choices=("auto", "on", "off"), default="auto",
-                    help="Qwen3-32B tensor-parallel decode tok/s (auto: only when N > 1)")
+    ap.add_argument("--tp-decode", choices=("on", "off"), default="on",
+                    help="Qwen3-32B tensor-parallel decode tok/s at TP = N (N = 1 is the "
+                         "single-GPU anchor of the curve) with token parity against one GPU")
     ap.add_argument("--tp-batches", default="1,8,32")
     ap.add_argument("--single", default=None,
                     help="N,K,M: run one decode linear --reps times and exit (profiler captures)")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--shapes", action="store_true",
                     help="per-shape table: every Qwen3-8B (M 1..16, verify 64..256) and Qwen3-0.6B "
-                         "(M 1..16) decode linear chained 20x in a graph, weights rotated beyond L2")
+                         "(M 1..16) decode linear chained 20x in a graph, weights rotated beyond "
+                         "L2, ours and torch.mm (cuBLAS)")
+    ap.add_argument("--split-sweep", action="store_true",
+                    help="Qwen3-8B decode linears at M 1 and 16 with split-K forced to 1..16")
+    ap.add_argument("--no-shapes", action="store_true",
+                    help="leave the per-shape table (ours vs torch.mm) out of the bench line")
     ap.add_argument("--attention", default=None,
                     help="B,KV: run --reps Qwen3-8B decode-attention launches (32 query / 8 KV "
                          "heads, synthetic cache of KV positions) on cuda:0 and exit")
@@ -325,6 +357,8 @@ def main():
         return attention_only(args)
     if args.shapes:
         return shapes_table(args)
+    if args.split_sweep:
+        return split_sweep(args)
     if args.decode_step:
         return decode_step_only(args)
     if args.warmup < 3:
@@ -494,13 +528,18 @@ def main():
                               world, local)
 
     tp_decode = None
-    if args.tp_decode == "on" or (args.tp_decode == "auto" and world > 1):
+    if args.tp_decode == "on":
         tp_decode = tp_decode_bench(nk, dev, [int(b) for b in args.tp_batches.split(",")],
                                     world, rank, local)
+
+    per_shape = None
+    if world == 1 and not args.no_shapes:
+        per_shape = shape_rows(dev, shape_cases())
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference(m_list, budget_s=args.cpu_budget)
+        cpu["config1"] = cpu_config1()
 
     if rank == 0:
         line = {
@@ -518,8 +557,10 @@ def main():
                        "plan_kinds": {str(k): v for k, v in by_kind.items()}},
             "per_m": per_m,
             "roofline": roofline,
-            "cpu_baseline": ({k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            "cpu_baseline": ({k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample",
+                                                   "config1")}
                              if cpu else None),
+            "per_shape": per_shape,
             "e2e": e2e,
             "decode": decode,
             "tp_decode": tp_decode,
@@ -558,47 +599,43 @@ QWEN3_0_6B_LINEARS = [("qkv", 4096, 1024), ("o_proj", 1024, 2048), ("gate_up", 6
                       ("down", 1024, 3072), ("lm_head", VOCAB, 1024)]
 
 
-def shapes_table(args, reps=5, chain=20):
+def shape_cases():
+    """(model, linear, N, K, M) of every per-shape row: Qwen3-8B decode (M 1..16), Qwen3-8B
+    tree verify (M 64..256), Qwen3-0.6B decode (M 1, 4, 8, 16)."""
+    cases = [("qwen3-8b", name, N, K, M) for name, N, K in LAYER_LINEARS + [("lm_head", VOCAB, HIDDEN)]
+             for M in (1, 2, 4, 8, 16)]
+    cases += [("qwen3-8b verify", name, N, K, M) for name, N, K in LAYER_LINEARS for M in (64, 128, 256)]
+    cases += [("qwen3-0.6b", name, N, K, M) for name, N, K in QWEN3_0_6B_LINEARS for M in (1, 4, 8, 16)]
+    return cases
+
+
+def shape_rows(dev, cases, reps=5, chain=20, cublas=True, split=0):
     """Per-shape decode-GEMM throughput as a decode step sees it: each (shape, M) launched
-    `chain` times in one CUDA graph (programmatic dependent launch between neighbours) with
+    ``chain`` times in one CUDA graph (programmatic dependent launch between neighbours) with
     its weight rotated over copies larger than 2 x L2, so every launch reads its weight from
-    DRAM. Prints one JSON line: us per launch, TB/s and the fraction of the measured HBM peak;
-    for the verify batches also TFLOP/s against the measured bf16 peak."""
+    DRAM; the same for torch.mm (cuBLAS, the reference's GPU path at engine/kernels/decode.py:
+    54-66) when ``cublas``. Rows carry us per launch, TB/s and the fraction of the measured HBM
+    peak, and for the verify batches TFLOP/s against the measured bf16 peak."""
     import neokernel_b200 as nk
     from neokernel_b200 import synthetic
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except Exception:
         peaks = {}
     hbm = float(peaks.get("hbm_gbs", 6650.0)) * 1e9
     tflops = float(peaks.get("bf16_tflops", 1590.0)) * 1e12
-    cases = [("qwen3-8b", name, N, K, M) for name, N, K in LAYER_LINEARS + [("lm_head", VOCAB, HIDDEN)]
-             for M in (1, 2, 4, 8, 16)]
-    cases += [("qwen3-8b verify", name, N, K, M) for name, N, K in LAYER_LINEARS for M in (64, 128, 256)]
-    cases += [("qwen3-0.6b", name, N, K, M) for name, N, K in QWEN3_0_6B_LINEARS for M in (1, 4, 8, 16)]
-    rows = []
     stream = torch.cuda.Stream(device=dev)
-    weights = {}
-    for model, name, N, K, M in cases:
-        if (N, K) not in weights:
-            weights.clear()
-            torch.cuda.empty_cache()
-            copies = max(2, (2 * 126 * 2 ** 20) // (N * K * 2) + 2)
-            weights[(N, K)] = [synthetic.weight(N, K, seed=i, device=dev) for i in range(copies)]
-        Ws = weights[(N, K)]
-        x = synthetic.activation(M, K, seed=M, device=dev)
-        y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-        plan = nk.plan_for(M, N, K)
+    weights, rows = {}, []
+
+    def timed(call):
         with torch.cuda.stream(stream):
             for W in Ws:
-                nk.mm(x, W.t(), out=y, plan=plan, stream=stream)
+                call(W)
         stream.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             for i in range(chain):
-                nk.mm(x, Ws[i % len(Ws)].t(), out=y, plan=plan, stream=stream)
+                call(Ws[i % len(Ws)])
         for _ in range(2):
             g.replay()
         torch.cuda.synchronize(dev)
@@ -609,19 +646,63 @@ def shapes_table(args, reps=5, chain=20):
                 g.replay()
             e1.record(stream)
         e1.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / (reps * chain)
+        del g
+        return e0.elapsed_time(e1) * 1e3 / (reps * chain)
+
+    def stats(us, M, N, K, prefix=""):
         b = gemm_bytes(M, N, K)
-        row = {"model": model, "linear": name, "N": N, "K": K, "M": M, "us": round(us, 2),
-               "TB/s": round(b / (us * 1e-6) / 1e12, 3), "hbm_frac": round(b / (us * 1e-6) / hbm, 3)}
+        r = {prefix + "us": round(us, 2), prefix + "TB/s": round(b / (us * 1e-6) / 1e12, 3),
+             prefix + "hbm_frac": round(b / (us * 1e-6) / hbm, 3)}
         if M >= 64:
             f = 2.0 * M * N * K
-            row["TFLOP/s"] = round(f / (us * 1e-6) / 1e12, 1)
-            row["tensor_frac"] = round(f / (us * 1e-6) / tflops, 3)
+            r[prefix + "TFLOP/s"] = round(f / (us * 1e-6) / 1e12, 1)
+            r[prefix + "tensor_frac"] = round(f / (us * 1e-6) / tflops, 3)
+        return r
+
+    for model, name, N, K, M in cases:
+        if (N, K) not in weights:
+            weights.clear()
+            torch.cuda.empty_cache()
+            copies = max(2, (2 * 126 * 2 ** 20) // (N * K * 2) + 2)
+            weights[(N, K)] = [synthetic.weight(N, K, seed=i, device=dev) for i in range(copies)]
+        Ws = weights[(N, K)]
+        x = synthetic.activation(M, K, seed=M, device=dev)
+        y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        plan = nk.plan_for(M, N, K, split_k=split)
+        row = {"model": model, "linear": name, "N": N, "K": K, "M": M}
+        row.update(stats(timed(lambda W: nk.mm(x, W.t(), out=y, plan=plan, stream=stream)), M, N, K))
+        if cublas:
+            row.update(stats(timed(lambda W: torch.mm(x, W.t(), out=y)), M, N, K, "cublas_"))
+            row["speedup_vs_cublas"] = round(row["cublas_us"] / row["us"], 3)
         rows.append(row)
-        del g
-    print(json.dumps({"shapes": rows, "timing": f"CUDA graph of {chain} launches per shape, "
-                      f"{reps} replays, CUDA events; weights rotated over > 2 x L2",
-                      "peaks": {"hbm_gbs": hbm / 1e9, "bf16_tflops": tflops / 1e12}}))
+    weights.clear()
+    torch.cuda.empty_cache()
+    return {"rows": rows, "timing": f"CUDA graph of {chain} launches per shape and arm, {reps} "
+            "replays, CUDA events; weights rotated over > 2 x L2",
+            "peaks": {"hbm_gbs": hbm / 1e9, "bf16_tflops": tflops / 1e12}}
+
+
+def shapes_table(args):
+    """--shapes: the per-shape table (ours and torch.mm) as one JSON line."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    print(json.dumps({"shapes": shape_rows(dev, shape_cases())}))
+    return 0
+
+
+def split_sweep(args):
+    """--split-sweep: the Qwen3-8B decode linears at M in {1, 16} with split-K forced to every
+    value 1..16 beside the plan's balanced schedule (split 0), us per launch as in shape_rows."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cases = [("qwen3-8b", name, N, K, M) for name, N, K in LAYER_LINEARS + [("lm_head", VOCAB, HIDDEN)]
+             for M in (1, 16)]
+    table = {}
+    for split in range(0, 17):
+        for r in shape_rows(dev, cases, reps=3, cublas=False, split=split)["rows"]:
+            table.setdefault(f"{r['linear']} M={r['M']}", {})[str(split)] = r["us"]
+    print(json.dumps({"split_sweep_us": table, "note": "split 0 = the plan's balanced "
+                      "persistent schedule; 1..16 = one CTA per (tile, K slice)"}))
     return 0
 
 
@@ -661,47 +742,261 @@ def attention_only(args):
     return 0
 
 
+REF_ENGINE_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+class _TorchWithMM:
+    """The ``torch`` module as engine/kernels/decode.py resolves it, with ``mm`` bound to another
+    implementation: the drop-in at the four linear call sites (decode.py:54,58,64,66) with the
+    reference's source unchanged."""
+
+    def __init__(self, mm):
+        self.mm = mm
+
+    def __getattr__(self, name):
+        return getattr(torch, name)
+
+
+def reference_engine():
+    """The reference's own decode kernels (engine/kernels: DecodeBuffers.layer with its Triton
+    norm, q/k-norm+RoPE+cache, split attention and SiLU kernels and its torch.mm linears),
+    installed unmodified into baseline/_ref. Returns (modules, None) or (None, why not)."""
+    if not os.path.isfile(os.path.join(REF_ENGINE_DIR, "kernels", "decode.py")):
+        return None, "the reference engine is not installed in baseline/_ref"
+    if REF_ENGINE_DIR not in sys.path:
+        sys.path.insert(0, REF_ENGINE_DIR)
+    try:
+        import kernels.decode as rdecode
+        import kernels.rmsnorm as rnorm
+        import kernels.weights as rweights
+    except Exception as e:  # report the exact import error in the bench line
+        return None, f"import of the reference engine failed: {type(e).__name__}: {e}"
+    return (rdecode, rweights, rnorm), None
+
+
+def _module_layer(lw, d):
+    """An object shaped like transformers' Qwen3DecoderLayer (the fields the reference's
+    LayerWeights reads, engine/kernels/weights.py:8-29) over one of our random-init layers."""
+    from types import SimpleNamespace as NS
+    D = d.head_dim
+    q_end, k_end = d.heads * D, d.heads * D + d.kv_heads * D
+    lin = lambda w: NS(weight=w, out_features=w.shape[0])  # noqa: E731
+    attn = NS(q_proj=lin(lw.qkv_weight[:q_end]), k_proj=lin(lw.qkv_weight[q_end:k_end]),
+              v_proj=lin(lw.qkv_weight[k_end:]), o_proj=lin(lw.o_weight),
+              q_norm=NS(weight=lw.q_norm), k_norm=NS(weight=lw.k_norm))
+    I = d.intermediate
+    mlp = NS(gate_proj=lin(lw.gate_up_weight[:I]), up_proj=lin(lw.gate_up_weight[I:]),
+             down_proj=lin(lw.down_weight))
+    return NS(self_attn=attn, mlp=mlp,
+              input_layernorm=NS(weight=lw.input_norm, variance_epsilon=d.eps),
+              post_attention_layernorm=NS(weight=lw.post_norm, variance_epsilon=d.eps))
+
+
+class ReferenceEngineDecoder:
+    """The reference engine's decode step, Engine.decode (engine/engine.py:100-117), driven on
+    its own DecodeBuffers.layer (engine/kernels/decode.py:42-68) with its shipped CONFIG
+    (fuse_norm_residual: carry_in/defer_out), its LayerWeights packing, cache_storage caches and
+    norm_out, captured in one CUDA graph as Engine.capture_decode does (side-stream warm-up x3,
+    engine/engine.py:119-129). Engine itself loads a checkpoint through transformers 4.51's
+    StaticCache, so the step is driven directly, as the reference's own layer test drives
+    DecodeBuffers.layer. DecodeBuffers has the Qwen3-4B widths built in (decode.py:27-37); for
+    another hidden/MLP width its x/norm/branch/gate_up/product/activation buffers are
+    re-allocated at that width, the only change. ``mm`` (default torch.mm, the reference as
+    shipped) is what the five linear call sites resolve to."""
+
+    def __init__(self, mods, w, batch, capacity, dev, mm=None):
+        rdecode, rweights, rnorm = mods
+        d = w.dims
+        self.d, self.batch = d, batch
+        self.mm = mm or torch.mm
+        self.norm_out = rnorm.norm_out
+        self.layers = [rweights.LayerWeights(_module_layer(lw, d)) for lw in w.layers]
+        self.embed, self.final_norm, self.lm_head = w.embed, w.final_norm, w.lm_head
+        buf = rdecode.DecodeBuffers(batch, capacity, dev)
+        bf = dict(device=dev, dtype=torch.bfloat16)
+        if d.hidden != buf.x.shape[1] or d.intermediate != buf.product.shape[1]:
+            for name, width in (("x", d.hidden), ("norm", d.hidden), ("branch", d.hidden),
+                                ("gate_up", 2 * d.intermediate), ("product", d.intermediate),
+                                ("activation", d.intermediate)):
+                setattr(buf, name, torch.empty(batch, width, **bf))
+        self.buf = buf
+        n = len(w.layers)
+        self.k = [rdecode.cache_storage(batch, capacity, dev, "bhsd") for _ in range(n)]
+        self.v = [rdecode.cache_storage(batch, capacity, dev, "bhsd") for _ in range(n)]
+        from neokernel_b200 import qwen3
+        self.cos, self.sin = qwen3.rope_tables(d, capacity, dev)
+        self.position = torch.zeros((1,), device=dev, dtype=torch.int64)
+        self.token_ids = torch.zeros((batch, 1), device=dev, dtype=torch.int64)
+        self.flat_tokens = self.token_ids.view(batch)
+        self.next_tokens = torch.zeros((batch, 1), device=dev, dtype=torch.int64)
+        self.logits = torch.empty((batch, d.vocab), **bf)
+        saved = rdecode.torch
+        rdecode.torch = _TorchWithMM(self.mm) if mm is not None else torch
+        try:
+            stream = torch.cuda.Stream(device=dev)
+            stream.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    self.decode()
+            torch.cuda.current_stream(dev).wait_stream(stream)
+            stream.synchronize()
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=stream):
+                self.decode()
+            torch.cuda.current_stream(dev).wait_stream(stream)
+        finally:
+            rdecode.torch = saved
+        self.reset()
+
+    def decode(self):
+        buf = self.buf
+        torch.index_select(self.embed, 0, self.flat_tokens, out=buf.x)
+        for i, lw in enumerate(self.layers):
+            buf.layer(lw, self.k[i], self.v[i], self.position, self.cos, self.sin,
+                      carry_in=i > 0, defer_out=True)
+        self.norm_out(buf.branch, self.final_norm, buf.norm, self.d.eps, buf.x, buf.x)
+        self.mm(buf.norm, self.lm_head, out=self.logits)
+        torch.argmax(self.logits, dim=-1, keepdim=True, out=self.next_tokens)
+
+    def reset(self):
+        for c in self.k + self.v:
+            c.zero_()
+        self.position.zero_()
+
+    def step(self):
+        self.graph.replay()
+        self.token_ids.copy_(self.next_tokens)
+        self.position.add_(1)
+
+    def greedy(self, prompt, new_tokens):
+        """Feed ``prompt`` [B, P] one token per step, then decode ``new_tokens`` greedily."""
+        self.reset()
+        B, P = prompt.shape
+        out = torch.empty(B, new_tokens, dtype=torch.int64, device=prompt.device)
+        for i in range(P):
+            self.token_ids[:, 0].copy_(prompt[:, i])
+            self.graph.replay()
+            self.position.add_(1)
+        self.token_ids.copy_(self.next_tokens)
+        for j in range(new_tokens):
+            out[:, j] = self.token_ids[:, 0]
+            if j + 1 < new_tokens:
+                self.step()
+        return out
+
+
+def _time_decoder(g, dev, kv, steps, warmup, world, local, vocab, B, seed):
+    """ms per decode step of a graph decoder (ours or the reference engine's) at KV length kv."""
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    caches = (g.st.k_cache + g.st.v_cache) if hasattr(g, "st") else (g.k + g.v)
+    for c in caches:
+        c.normal_(generator=gen)
+    pos = g.st.position if hasattr(g, "st") else g.position
+    tok = g.st.tokens if hasattr(g, "st") else g.flat_tokens
+    pos.fill_(kv)
+    tok.copy_(torch.randint(0, vocab, (B,), generator=gen, device=dev))
+    for _ in range(warmup):
+        g.step()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    a.record()
+    for _ in range(steps):
+        g.step()
+    b.record()
+    b.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b), world, local) / steps
+    return {"ms_per_token_step": round(ms, 4), "tok_s": round(B * world / (ms / 1e3), 1)}
+
+
 def decode_bench(nk, dev, batches, world, local, kv=1024, steps=20, warmup=3):
-    """Decode tokens/s of the full Qwen3-8B step (36 layers, random init, CUDA graph) at KV
-    length 1024. Arms: the product (fused non-linear kernels, neokernel_b200.mm and the fused
-    lm_head + argmax), the same
-    fused step with the linears on torch.mm (cuBLAS, the reference's call), and the step with
-    PyTorch non-linear ops and torch.mm."""
+    """Decode tokens/s of the full Qwen3-8B step (36 layers, decisive random init, CUDA graph)
+    at KV length 1024. Arms:
+    * neokernel_b200: the product — fused decode kernels, neokernel_b200.mm and the fused
+      lm_head + argmax;
+    * fused_ops_torch_mm: the same fused step with the linears on torch.mm (cuBLAS);
+    * torch_ops_torch_mm: PyTorch non-linear ops and torch.mm;
+    * reference_triton (N = 1): the reference engine's own decode step — its Triton kernels and
+      torch.mm linears (ReferenceEngineDecoder);
+    * reference_triton_nk_mm (N = 1): the same reference step with neokernel_b200.mm at its
+      five linear call sites, the documented drop-in;
+    and, at N = 1, greedy-token parity of the product against the reference engine, plus the
+    Qwen3-4B widths the reference's DecodeBuffers has built in."""
     from neokernel_b200 import qwen3
     w = qwen3.Qwen3Weights(qwen3.QWEN3_8B, seed=7, device=dev)
-    out = {"model": "qwen3-8b random-init, 36 layers, vocab 151936", "kv_length": kv,
+    out = {"model": "qwen3-8b decisive random init, 36 layers, vocab 151936", "kv_length": kv,
            "steps": steps, "timing": "CUDA events around graph replays, max over ranks"}
-    arms = (("neokernel_b200", nk.mm, True), ("fused_ops_torch_mm", torch.mm, True),
-            ("torch_ops_torch_mm", torch.mm, False))
-    for name, linear, fused in arms:
-        res = {}
-        for B in batches:
-            g = qwen3.GraphDecoder(w, B, kv + warmup + steps + 1, linear, device=dev,
-                                   fused=fused, fused_head=linear is nk.mm)
-            gen = torch.Generator(device=dev).manual_seed(B)
-            for c in g.st.k_cache + g.st.v_cache:
-                c.normal_(generator=gen)
-            g.st.position.fill_(kv)
-            g.st.tokens.copy_(torch.randint(0, qwen3.QWEN3_8B.vocab, (B,), generator=gen, device=dev))
-            for _ in range(warmup):
-                g.step()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            barrier(world)
-            torch.cuda.synchronize(dev)
-            a.record()
-            for _ in range(steps):
-                g.step()
-            b.record()
-            b.synchronize()
-            ms = max_over_ranks(a.elapsed_time(b), world, local) / steps
-            res[str(B)] = {"ms_per_token_step": round(ms, 4),
-                           "tok_s": round(B * world / (ms / 1e3), 1)}
-            del g
-            torch.cuda.empty_cache()
-        out[name] = res
-    del w
+    mods, why = reference_engine() if world == 1 else (None, "single-GPU comparison only")
+
+    def ours(w, B, linear, fused, fused_head):
+        return qwen3.GraphDecoder(w, B, kv + warmup + steps + 1, linear, device=dev,
+                                  fused=fused, fused_head=fused_head)
+
+    def ref_engine(w, B, mm=None):
+        return ReferenceEngineDecoder(mods, w, B, kv + warmup + steps + 1, dev, mm=mm)
+
+    arms = [("neokernel_b200", lambda w, B: ours(w, B, nk.mm, True, True)),
+            ("fused_ops_torch_mm", lambda w, B: ours(w, B, torch.mm, True, False)),
+            ("torch_ops_torch_mm", lambda w, B: ours(w, B, torch.mm, False, False))]
+    ref_arms = [("reference_triton", lambda w, B: ref_engine(w, B)),
+                ("reference_triton_nk_mm", lambda w, B: ref_engine(w, B, nk.mm))]
+
+    def run_arms(w, arms, into):
+        for name, make in arms:
+            res = {}
+            for B in batches:
+                try:
+                    g = make(w, B)
+                except Exception as e:  # the reference engine's arms report why they failed
+                    if not name.startswith("reference"):
+                        raise
+                    res = {"unavailable": f"{type(e).__name__}: {str(e)[:300]}"}
+                    break
+                res[str(B)] = _time_decoder(g, dev, kv, steps, warmup, world, local,
+                                            w.dims.vocab, B, seed=B)
+                del g
+                torch.cuda.empty_cache()
+            into[name] = res
+
+    run_arms(w, arms, out)
+    if mods is None:
+        for name, _ in ref_arms:
+            out[name] = {"unavailable": why}
+    else:
+        run_arms(w, ref_arms, out)
+        out["reference_engine_parity"] = _engine_parity(mods, w, nk, dev)
+        del w
+        torch.cuda.empty_cache()
+        w4 = qwen3.Qwen3Weights(qwen3.QWEN3_4B, seed=7, device=dev)
+        out4 = {"model": "qwen3-4b random init (tied embeddings), 36 layers: the widths the "
+                         "reference's DecodeBuffers has built in"}
+        run_arms(w4, arms[:1] + ref_arms, out4)
+        out["qwen3_4b"] = out4
+        del w4
     torch.cuda.empty_cache()
     return out
+
+
+def _engine_parity(mods, w, nk, dev, batch=4, prompt_len=8, new=32):
+    """Greedy tokens of the product step against the reference engine's own step (its Triton
+    kernels and torch.mm) on the same weights and prompt."""
+    from neokernel_b200 import qwen3
+    cap = prompt_len + new
+    gen = torch.Generator(device=dev).manual_seed(2026)
+    prompt = torch.randint(0, w.dims.vocab, (batch, prompt_len), generator=gen, device=dev)
+    ref = ReferenceEngineDecoder(mods, w, batch, cap, dev)
+    t_ref = ref.greedy(prompt, new)
+    del ref
+    ours = qwen3.GraphDecoder(w, batch, cap, nk.mm, device=dev, fused=True, fused_head=True)
+    t_ours = ours.greedy(prompt, new)
+    del ours
+    torch.cuda.synchronize(dev)
+    eq = t_ours == t_ref
+    first = [int((~eq[b]).nonzero()[0]) if not eq[b].all() else None for b in range(batch)]
+    return {"tokens_equal": bool(eq.all()), "identical_tokens": int(eq.sum()),
+            "tokens": batch * new, "batch": batch, "first_divergence": first,
+            "arms": "neokernel_b200 product step vs the reference engine's DecodeBuffers.layer "
+                    "step (Triton + torch.mm), same weights and prompt"}
 
 
 def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, warmup=3):
@@ -716,6 +1011,7 @@ def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, war
     d = qwen3.QWEN3_32B
     w = tp.TPWeights(d, seed=13, rank=rank, world=world, device=dev)
     arms = ("auto", "nccl") if world > 1 else ("auto",)
+    # all ranks take every collective step below in the same order
     out = {}
     for collective in arms:
         res = {}
@@ -747,13 +1043,46 @@ def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, war
         out[collective] = res
     del w
     torch.cuda.empty_cache()
+    parity = _tp_parity(nk, dev, world, rank, local)
     return {"model": "qwen3-32b random-init, 64 layers, hidden 5120, MLP 25600, 64Q/8KV x 128",
             "tp": world, "kv_length": kv, "steps": steps, "batches": out["auto"],
+            "tp_parity": parity,
             "batches_nccl_allreduce": out.get("nccl"),
             "collectives": "fp32 partials of o_proj and down summed across ranks, one bf16 "
                            "rounding: nk_allreduce_bf16 over NVLink peer memory (rank order) up "
                            "to 64K elements, NCCL all-reduce above; NCCL all-gather of (max, "
                            "index) for the vocab-split argmax; all captured in the CUDA graph"}
+
+
+def _tp_parity(nk, dev, world, rank, local, layers=4, batch=4, prompt_len=8, new=24):
+    """Greedy tokens of the tensor-parallel product step (this run's TP = N, fused kernels,
+    collectives, per-shard greedy head) against the single-GPU product step of the same model
+    — Qwen3-32B shapes with ``layers`` layers and the decisive init — decoded on every rank
+    from the same prompt. ``tokens_equal`` holds only if it holds on every rank."""
+    from neokernel_b200 import qwen3, tp
+    d = qwen3.QWEN3_32B
+    cap = prompt_len + new
+    gen = torch.Generator(device=dev).manual_seed(4242)
+    prompt = torch.randint(0, d.vocab, (batch, prompt_len), generator=gen, device=dev)
+    full = qwen3.Qwen3Weights(d, seed=17, device=dev, layers=layers)
+    one = qwen3.GraphDecoder(full, batch, cap, nk.mm, device=dev, fused=True, fused_head=True)
+    t_one = one.greedy(prompt, new)
+    del one, full
+    shard = tp.TPWeights(d, seed=17, rank=rank, world=world, device=dev, layers=layers)
+    g = qwen3.GraphDecoder(shard, batch, cap, nk.mm, device=dev, fused=True,
+                           make_hooks=tp.make_hooks(shard))
+    t_tp = g.greedy(prompt, new)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    del g.graph  # a graph holding NCCL calls goes before anything tears the group down
+    del g, shard
+    torch.cuda.empty_cache()
+    same = int((t_tp == t_one).sum())
+    worst = -max_over_ranks(-float(same), world, local)  # min over ranks
+    return {"tokens_equal": worst == batch * new, "identical_tokens_min_over_ranks": int(worst),
+            "tokens": batch * new, "batch": batch, "layers": layers, "tp": world,
+            "against": "the single-GPU product step of the same Qwen3-32B-shaped model "
+                       "(decisive init), on every rank"}
 
 
 def decode_step_only(args, kv=1024):

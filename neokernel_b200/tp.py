@@ -15,8 +15,9 @@ shards the decode linears where their weights shard naturally:
   buffer over NVLink and adds the ranks in rank order; ``collective="nccl"`` uses NCCL's
   all-reduce instead (and CPU process groups always use ``dist.all_reduce``);
 * lm_head (engine.py:114) is split by vocabulary row: each rank takes its local max and its
-  lowest index, and an all-gather of (value, index) picks the global maximum, ties to the
-  lowest vocabulary index as torch.argmax does (engine.py:116).
+  lowest index — on GPUs in the lm_head launch itself (``mm_argmax``, the fused greedy head),
+  so the [B, vocab / T] logits are not stored — and an all-gather of (value, index) picks the
+  global maximum, ties to the lowest vocabulary index as torch.argmax does (engine.py:116).
 
 Embedding and norms are replicated. Every rank issues the same collectives in the same order
 in warm-up, capture and replay. The weights of a rank are the slices of exactly the matrices
@@ -99,7 +100,8 @@ class TPWeights:
 PEER_MAX_AUTO = 1 << 16  # fp32 elements up to which "auto" sums partials over peer memory
 
 
-def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None, collective="auto"):
+def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None, collective="auto",
+               fused_head: bool = True):
     """Return ``make(state) -> (row_linear, head)`` for ``qwen3.GraphDecoder`` / ``decode_step``.
 
     ``linear_f32(a, b, out)`` computes an unrounded fp32 partial (default:
@@ -108,8 +110,10 @@ def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None, collectiv
     (``nk_allreduce_bf16`` over NVLink peer memory), "nccl" (``dist.all_reduce``, then the bf16
     copy) or "auto": peer on a CUDA process group of 2+ ranks for partials of up to
     ``PEER_MAX_AUTO`` elements, else all_reduce (measured on B200, Qwen3-32B TP=2: the peer
-    sum is ahead at batch 1 and behind NCCL at batch 32). Buffers are allocated here, once per
-    state, so the hooks are capture-safe.
+    sum is ahead at batch 1 and behind NCCL at batch 32). ``fused_head`` (CUDA states only)
+    takes each rank's (max, lowest index) from the lm_head launch (``neokernel_b200.mm_argmax``)
+    instead of storing the logits and reducing them; ``state.logits`` is then left untouched.
+    Buffers are allocated here, once per state, so the hooks are capture-safe.
     """
     if collective not in ("auto", "peer", "nccl"):
         raise ValueError(f"collective must be auto, peer or nccl, not {collective!r}")
@@ -130,6 +134,8 @@ def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None, collectiv
             from .peer import PeerGroup
             peer = PeerGroup(B * H, group=group, device=dev)
         partial = torch.empty(B, H, device=dev, dtype=torch.float32)
+        use_fused_head = fused_head and dev.type == "cuda"
+        best_bf16 = torch.empty(B, device=dev, dtype=torch.bfloat16)
         best = torch.empty(B, device=dev, dtype=torch.float32)
         best_idx = torch.empty(B, device=dev, dtype=torch.int64)
         all_best = torch.empty(world * B, device=dev, dtype=torch.float32)
@@ -145,8 +151,14 @@ def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None, collectiv
             out.copy_(partial)  # the one rounding to bf16 (nearest-even)
 
         def head(state, lm_head, _linear):
-            linear(state.norm, lm_head, out=state.logits)
-            torch.max(state.logits.float(), dim=-1, out=(best, best_idx))  # first max index
+            if use_fused_head:
+                from .gemm import mm_argmax
+                # this shard's lowest-index maximum, from the lm_head launch itself
+                mm_argmax(state.norm, lm_head, idx=best_idx, best=best_bf16)
+                best.copy_(best_bf16)  # exact: every bf16 value is an fp32 value
+            else:
+                linear(state.norm, lm_head, out=state.logits)
+                torch.max(state.logits.float(), dim=-1, out=(best, best_idx))  # first max index
             best_idx.add_(vocab_offset)
             if world > 1:
                 dist.all_gather_into_tensor(all_best, best, group=group)

@@ -41,14 +41,19 @@ def _worker(rank, world, port, q, collective):
         shard = tp.TPWeights(d, seed=21, rank=rank, world=world, device=dev, layers=layers)
         B, cap = 4, 32
         ref = qwen3.GraphDecoder(full, B, cap, nk.mm, device=dev)
+        # logits stored (lm_head, then torch.max of the shard) ...
         tpg = qwen3.GraphDecoder(shard, B, cap, nk.mm, device=dev,
+                                 make_hooks=tp.make_hooks(shard, collective=collective,
+                                                          fused_head=False))
+        # ... and the product hook: each shard's argmax from the lm_head launch itself
+        tpf = qwen3.GraphDecoder(shard, B, cap, nk.mm, device=dev, fused=True,
                                  make_hooks=tp.make_hooks(shard, collective=collective))
         gen = torch.Generator(device=dev).manual_seed(77)
         worst, agree, total = 0.0, 0, 0
         vl = d.vocab // world
         for pos in range(8):
             toks = torch.randint(0, d.vocab, (B,), generator=gen, device=dev)
-            for g in (ref, tpg):
+            for g in (ref, tpg, tpf):
                 g.st.tokens.copy_(toks)
                 g.st.position.fill_(pos)
                 g.graph.replay()
@@ -58,8 +63,9 @@ def _worker(rank, world, port, q, collective):
             top2 = ref.st.logits.float().topk(2, dim=-1).values
             decisive = (top2[:, 0] - top2[:, 1]) > 0.1
             agree += int((tpg.st.next_tokens == ref.st.next_tokens)[decisive].sum())
-            total += int(decisive.sum())
-        del ref.graph, tpg.graph  # graphs holding NCCL calls go before the process group
+            agree += int((tpf.st.next_tokens == ref.st.next_tokens)[decisive].sum())
+            total += 2 * int(decisive.sum())
+        del ref.graph, tpg.graph, tpf.graph  # graphs holding NCCL calls go before the group
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, "ok", worst, agree, total))
