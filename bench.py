@@ -327,6 +327,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true",
                     help="skip the 36-layer Qwen3-8B decode-step tok/s measurement")
     ap.add_argument("--decode-batches", default="1,16")
+    ap.add_argument("--decode-arms", default="all",
+                    help="comma list of decode arms to time (default all; e.g. neokernel_b200)")
     ap.add_argument("--tp-decode", choices=("on", "off"), default="on",
                     help="Qwen3-32B tensor-parallel decode tok/s at TP = N (N = 1 is the "
                          "single-GPU anchor of the curve) with token parity against one GPU")
@@ -525,7 +527,7 @@ def main():
     decode = None
     if not args.no_decode:
         decode = decode_bench(nk, dev, [int(b) for b in args.decode_batches.split(",")],
-                              world, local)
+                              world, local, arms_filter=args.decode_arms)
 
     tp_decode = None
     if args.tp_decode == "on":
@@ -909,7 +911,7 @@ def _time_decoder(g, dev, kv, steps, warmup, world, local, vocab, B, seed):
     return {"ms_per_token_step": round(ms, 4), "tok_s": round(B * world / (ms / 1e3), 1)}
 
 
-def decode_bench(nk, dev, batches, world, local, kv=1024, steps=20, warmup=3):
+def decode_bench(nk, dev, batches, world, local, kv=1024, steps=20, warmup=3, arms_filter="all"):
     """Decode tokens/s of the full Qwen3-8B step (36 layers, decisive random init, CUDA graph)
     at KV length 1024. Arms:
     * neokernel_b200: the product — fused decode kernels, neokernel_b200.mm and the fused
@@ -958,6 +960,12 @@ def decode_bench(nk, dev, batches, world, local, kv=1024, steps=20, warmup=3):
                 torch.cuda.empty_cache()
             into[name] = res
 
+    if arms_filter != "all":
+        keep = set(arms_filter.split(","))
+        arms = [a for a in arms if a[0] in keep]
+        ref_arms = [a for a in ref_arms if a[0] in keep]
+        if not ref_arms:
+            mods, why = None, "not requested"
     run_arms(w, arms, out)
     if mods is None:
         for name, _ in ref_arms:

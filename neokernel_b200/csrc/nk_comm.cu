@@ -1,4 +1,5 @@
-// One-shot all-reduce of fp32 partials over NVLink peer memory (include/nk_comm.h).
+// One-shot all-reduce of fp32 partials over NVLink peer memory (include/nk_comm.h), launched
+// with programmatic dependent launch so it starts while the GEMM that made the partial drains.
 //
 // Buffer of one rank (zeroed once, mapped into every rank of the group):
 //   [0, 4 KB)            progress counter of each CTA index (read and advanced by that CTA)
@@ -54,6 +55,10 @@ allreduce_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ o
                       PeerArgs g) {
     __shared__ unsigned s_e;
     __shared__ int s_ok;
+    // Launched with programmatic dependent launch: the partial x comes from the previous
+    // kernel (and this CTA's epoch counter from the previous call), so wait before any read.
+    if (threadIdx.x == 0) griddep_launch_dependents();
+    griddep_wait();
     const int c = blockIdx.x;
     uint8_t* own = g.buf[g.rank];
     unsigned* epo = reinterpret_cast<unsigned*>(own) + c;
@@ -177,7 +182,6 @@ extern "C" int nk_allreduce_bf16(const float* x, void* out, int n, const nk_peer
     a.world = g->world;
     a.max_elems = g->max_elems;
     const int grid = (n + kArElemsPerCta - 1) / kArElemsPerCta;
-    allreduce_bf16_kernel<<<grid, kArThreads, 0, (cudaStream_t)stream>>>(
-        x, static_cast<__nv_bfloat16*>(out), n, a);
-    return cudaGetLastError() == cudaSuccess ? NK_OK : NK_ERR_CUDA;
+    return launch_pdl_smem(allreduce_bf16_kernel, dim3(grid), dim3(kArThreads), 0,
+                           (cudaStream_t)stream, x, static_cast<__nv_bfloat16*>(out), n, a);
 }

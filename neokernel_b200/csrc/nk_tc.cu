@@ -225,7 +225,8 @@ struct TcSmem {
     static constexpr int kStagesFit = (kBudget - 2048) / kStage;
     static constexpr int kStages = kStagesFit > 8 ? 8 : (kStagesFit < 2 ? 2 : kStagesFit);
     static constexpr int kBarOff = kStages * kStage;
-    static constexpr int kNumBars = 2 * kStages + 6;     // full, empty, tfull[2], tempty[2], part[2]
+    static constexpr int kPartBars = 8;                  // partial chunks in flight (finisher)
+    static constexpr int kNumBars = 2 * kStages + 4 + kPartBars;  // full, empty, tfull[2], tempty[2], part
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
     static constexpr int kBytes = kMiscOff + 16;         // tmem slot, abort flag, last flag
     static constexpr int kAlloc = kBytes + 1024;         // slack to align the base to 1 KB
@@ -443,8 +444,8 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar_tfull + 8 * i, 1);
             mbar_init(bar_tempty + 8 * i, kTcEpiThreads / 32);
-            mbar_init(bar_part + 8 * i, 1);
         }
+        for (int i = 0; i < L::kPartBars; ++i) mbar_init(bar_part + 8 * i, 1);
         *abort_flag = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -654,40 +655,43 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             } else {
                 // own + (rank 1 + rank 2 + ...): a fixed order, whichever rank is late
                 constexpr uint32_t kChunkBytes = 16u * kTcRows * 4u;  // 16 columns of one rank
-                constexpr uint32_t kHalf = (uint32_t)(STAGES * L::kStage) / 2u;
+                constexpr uint32_t kRing = (uint32_t)(STAGES * L::kStage);
                 const int partners = nseg - 1;
-                const bool bulk = NT != 16 && !tagged && got && partners >= 1 &&
-                                  (uint32_t)partners * kChunkBytes <= kHalf;
+                const int nchunks = (mcount + 15) / 16;
+                // chunk slots in the idle ring: as many chunks in flight as fit (and barriers)
+                int slots = partners >= 1 ? (int)(kRing / ((uint32_t)partners * kChunkBytes)) : 0;
+                slots = slots < L::kPartBars ? slots : L::kPartBars;
+                slots = slots < nchunks ? slots : nchunks;
+                const bool bulk = NT != 16 && !tagged && got && slots >= 1;
                 if (ok && bulk) {
                     // Every MMA of this CTA is done, so the shared-memory ring is idle: pull each
                     // partner's partial columns [16k, 16k + 16) — contiguous fp32, [column][128
-                    // rows] — with one bulk copy per rank into alternate halves of the ring, two
-                    // chunks in flight, and add them from shared memory.
+                    // rows] — with one bulk copy per rank into slot k % slots of the ring, up to
+                    // `slots` chunks in flight, and add them from shared memory.
+                    const uint32_t slot_bytes = (uint32_t)partners * kChunkBytes;
                     const float* tile_part =
                         a.part + ((size_t)sg.t * a.segments * a.part_cols) * kTcRows;
-                    const int nchunks = (mcount + 15) / 16;
                     auto issue = [&](int k) {  // one thread
-                        const int h = k & 1;
+                        const int h = k % slots;
                         const int cols = min(16, a.part_cols - 16 * k);  // never past the tile
                         const uint32_t bytes = (uint32_t)cols * kTcRows * 4u;
                         mbar_expect_tx(bar_part + 8 * h, (uint32_t)partners * bytes);
                         for (int i = 0; i < partners; ++i)
-                            bulk_load(base + h * kHalf + (uint32_t)i * kChunkBytes,
+                            bulk_load(base + h * slot_bytes + (uint32_t)i * kChunkBytes,
                                       tile_part + ((size_t)(1 + i) * a.part_cols + 16 * k) * kTcRows,
                                       bytes, bar_part + 8 * h);
                     };
-                    if (ep == 0) {
-                        issue(0);
-                        if (nchunks > 1) issue(1);
-                    }
+                    if (ep == 0)
+                        for (int k = 0; k < slots; ++k) issue(k);
 #pragma unroll 1
                     for (int k = 0; k < nchunks; ++k) {
-                        const int h = k & 1;
-                        const bool arrived =
-                            __all_sync(0xffffffffu, mbar_wait(bar_part + 8 * h, (uint32_t)(k >> 1) & 1u));
+                        const int h = k % slots;
+                        const bool arrived = __all_sync(
+                            0xffffffffu, mbar_wait(bar_part + 8 * h, (uint32_t)(k / slots) & 1u));
                         float v[16];
                         tmem_ld16(taddr + 16 * k, v);
-                        const float* sm = reinterpret_cast<const float*>(gbase + h * kHalf) + row;
+                        const float* sm =
+                            reinterpret_cast<const float*>(gbase + h * slot_bytes) + row;
                         float ps[16];
 #pragma unroll
                         for (int j = 0; j < 16; ++j) ps[j] = 0.f;
@@ -705,10 +709,12 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                         if constexpr (AMAX)
                             amax_fold16(a, arrived && n < a.N, n, m0 + 16 * k,
                                         min(16, mcount - 16 * k), v);
-                        epi_bar();  // every thread is done with this half
-                        if (ep == 0 && k + 2 < nchunks) {
-                            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                            issue(k + 2);
+                        if (k + slots < nchunks) {
+                            epi_bar();  // every thread is done with this slot
+                            if (ep == 0) {
+                                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                                issue(k + slots);
+                            }
                         }
                     }
                 } else if (ok) {

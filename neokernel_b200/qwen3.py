@@ -325,6 +325,9 @@ class GraphDecoder:
         row_linear, head = make_hooks(self.st) if make_hooks else (None, None)
         if fused_head and head is None:
             head = fused_greedy_head
+        # The captured graph holds raw pointers into the buffers these hooks own (partial sums,
+        # per-shard maxima, peer buffers), so the hooks live exactly as long as the graph.
+        self.hooks = (row_linear, head)
         step = lambda: decode_step(self.st, w, linear, row_linear, head, fused)  # noqa: E731
         stream = torch.cuda.Stream(device=device)
         self.stream = stream

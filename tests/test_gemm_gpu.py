@@ -340,6 +340,7 @@ def test_graph_survives_workspace_growth_on_its_stream():
     xh = synthetic.activation(16, K, seed=64, device=DEV)
     yh = torch.empty((16, Nh), dtype=torch.bfloat16, device=DEV)
     idx = torch.empty((16, 1), dtype=torch.int64, device=DEV)
+    stream.wait_stream(torch.cuda.current_stream())  # the inputs were made on this stream
     with torch.cuda.stream(stream):
         nk.mm(xh, Wh.t(), out=yh)
         nk.mm_argmax(xh, Wh.t(), idx=idx)
@@ -381,3 +382,18 @@ def test_shim_errors_on_gpu():
 def test_no_device_error_left():
     torch.cuda.synchronize()
     assert nk.device_error() == 0
+
+
+@pytest.mark.parametrize("N,K", [(5120, 8192), (5120, 1024), (5120, 25600), (5120, 3200)])
+@pytest.mark.parametrize("M", (1, 4, 8, 32))
+def test_f32_output_is_the_unrounded_sum(M, N, K):
+    """mm_f32 (nk_gemm_bf16_f32out), the K-split partial of the tensor-parallel o_proj/down:
+    the same fp32 sums mm rounds, so rounding it to bf16 gives mm's output bit for bit."""
+    W = weight_dev(N, K, seed=N + 3 * K)
+    x = synthetic.activation(M, K, seed=M + 7, device=DEV)
+    y = run(x, W)
+    p = torch.empty((M, N), dtype=torch.float32, device=DEV)
+    nk.mm_f32(x, W.t(), out=p)
+    assert torch.equal(p.to(torch.bfloat16), y)
+    # fp32 against fp32 (TF32 off): only the order of the additions differs
+    assert (p - fp32_ref(x, W)).abs().max().item() <= 1e-3
