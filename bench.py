@@ -1011,14 +1011,14 @@ def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, war
     """Qwen3-32B-shaped tensor-parallel decode (64 layers, random init) over the N ranks of
     this run: QKV/gate_up split by column, o_proj/down by K with their fp32 partials summed
     across ranks, lm_head by vocabulary; one CUDA graph per batch; KV length 2048. The
-    product ("auto") sums the partials with the peer-memory all-reduce (nk_allreduce_bf16) for
-    small batches and NCCL's all-reduce for large ones; at N > 1 the step with NCCL's
-    all-reduce throughout is timed beside it. tok/s counts each sequence's token once (the
-    ranks share one model)."""
+    product ("auto") fuses each K-slice linear with the rank-order sum over NVLink peer memory
+    (nk_gemm_bf16_allreduce) for batches up to 64; at N > 1 the step with the unfused pair
+    (mm_f32, nk_allreduce_bf16) and with NCCL's all-reduce are timed beside it. tok/s counts
+    each sequence's token once (the ranks share one model)."""
     from neokernel_b200 import qwen3, tp
     d = qwen3.QWEN3_32B
     w = tp.TPWeights(d, seed=13, rank=rank, world=world, device=dev)
-    arms = ("auto", "nccl") if world > 1 else ("auto",)
+    arms = ("auto", "peer", "nccl") if world > 1 else ("auto",)
     # all ranks take every collective step below in the same order
     out = {}
     for collective in arms:
@@ -1055,11 +1055,14 @@ def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, war
     return {"model": "qwen3-32b random-init, 64 layers, hidden 5120, MLP 25600, 64Q/8KV x 128",
             "tp": world, "kv_length": kv, "steps": steps, "batches": out["auto"],
             "tp_parity": parity,
+            "batches_unfused_peer_allreduce": out.get("peer"),
             "batches_nccl_allreduce": out.get("nccl"),
-            "collectives": "fp32 partials of o_proj and down summed across ranks, one bf16 "
-                           "rounding: nk_allreduce_bf16 over NVLink peer memory (rank order) up "
-                           "to 64K elements, NCCL all-reduce above; NCCL all-gather of (max, "
-                           "index) for the vocab-split argmax; all captured in the CUDA graph"}
+            "collectives": "o_proj and down: each rank's K slice fused with the rank-order sum "
+                           "over NVLink peer memory in one launch (nk_gemm_bf16_allreduce) for "
+                           "batches up to 64; the 'peer' arm launches mm_f32 then "
+                           "nk_allreduce_bf16, the 'nccl' arm mm_f32 then NCCL all-reduce; "
+                           "lm_head: each shard's argmax in its launch (nk_gemm_bf16_argmax), "
+                           "NCCL all-gather of (max, index); all captured in the CUDA graph"}
 
 
 def _tp_parity(nk, dev, world, rank, local, layers=4, batch=4, prompt_len=8, new=24):

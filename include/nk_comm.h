@@ -63,6 +63,30 @@ NK_API int nk_ipc_close(void* ptr);
 NK_API int nk_allreduce_bf16(const float* x, void* out, int n, const nk_peer_group* g,
                              nk_stream_t stream);
 
+/*
+ * The K-split linear of a tensor-parallel group fused with its all-reduce, in one launch per
+ * rank: y = bf16( sum over ranks r, in rank order, of x_r · W_rᵀ ), where x_r · W_rᵀ is this
+ * rank's fp32 partial (the nk_gemm_bf16_f32out product) and the group holds one rank per K
+ * slice. As each output tile's fp32 values are final, the CTA that made them stores them into
+ * every rank's receive buffer over NVLink (plain peer stores), publishes the tile's call number
+ * to every rank, waits (bounded, about 2 s; NK_ERR_TIMEOUT through nk_device_error) for every
+ * rank's, and stores the rank-order sum of the tile rounded once to bf16 — the bits
+ * nk_gemm_bf16_f32out followed by nk_allreduce_bf16 give, without the second launch or a
+ * separate pass over the partial. Replaces the pair mm_f32 + all-reduce of the library's
+ * tensor-parallel o_proj / down (the split forms of engine/kernels/decode.py:58,66; the
+ * reference itself is single-GPU, engine/engine.py:65).
+ *   Arguments as nk_gemm_bf16 (y bf16 [M, N], row stride ldy; ws as nk_ws_bytes(plan)), plus
+ *   the group, whose receive buffers must hold M * N elements (max_elems) and which serves no
+ *   nk_allreduce_bf16 calls. Plans: the balanced tensor-core schedule (split_k 0, the AUTO
+ *   choice for aligned shapes) with token tiles of up to 64 (M_max <= 64) and at most 1024
+ *   output tiles; else NK_ERR_PLAN. Every rank makes the same sequence of calls, each on one
+ *   stream, with the same plan; calls are CUDA-graph capturable.
+ */
+NK_API int nk_gemm_bf16_allreduce(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                  void* y, int64_t ldy, int M, int N, int K,
+                                  const nk_plan* plan, void* ws, size_t ws_bytes,
+                                  const nk_peer_group* g, nk_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

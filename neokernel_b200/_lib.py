@@ -40,7 +40,8 @@ EXPORTS = ("nk_plan_make", "nk_ws_bytes", "nk_ws_init", "nk_gemm_bf16", "nk_devi
            "nk_rmsnorm_bf16", "nk_qk_norm_rope_cache_bf16", "nk_attention_ws_bytes",
            "nk_attention_decode_bf16", "nk_silu_mul_bf16", "nk_peer_buffer_bytes", "nk_peer_alloc",
            "nk_peer_free", "nk_ipc_handle", "nk_ipc_open", "nk_ipc_close", "nk_allreduce_bf16",
-           "nk_gemm_argmax_ws_bytes", "nk_gemm_bf16_argmax", "nk_test_withhold_partial")
+           "nk_gemm_argmax_ws_bytes", "nk_gemm_bf16_argmax", "nk_test_withhold_partial",
+           "nk_gemm_bf16_allreduce")
 
 
 NK_PEER_MAX_RANKS = 8
@@ -149,6 +150,10 @@ def load() -> ctypes.CDLL:
     L.nk_allreduce_bf16.restype = i32
     L.nk_test_withhold_partial.argtypes = [i32]
     L.nk_test_withhold_partial.restype = i32
+    L.nk_gemm_bf16_allreduce.argtypes = [vp, i64, vp, i64, vp, i64, i32, i32, i32,
+                                         ctypes.POINTER(NkPlan), vp, ctypes.c_size_t,
+                                         ctypes.POINTER(NkPeerGroup), vp]
+    L.nk_gemm_bf16_allreduce.restype = i32
     L.nk_device_error.argtypes = [vp, ctypes.POINTER(i32)]
     L.nk_device_error.restype = i32
     L.nk_status_string.argtypes = [i32]

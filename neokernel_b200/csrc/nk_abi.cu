@@ -172,6 +172,12 @@ struct AmaxOut {
     void* best;
 };
 
+// The tensor-parallel group of the fused all-reduce (nk_gemm_bf16_allreduce), validated.
+struct ArIn {
+    void* buf[NK_PEER_MAX_RANKS_INTERNAL];
+    int rank, world, max_elems;
+};
+
 // Every check of a linear's arguments that involves neither the workspace nor the device
 // (plan, shape, pointers, alignment). Returns NK_OK or the NK_ERR_* the entry point reports.
 static int gemm_validate(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* y,
@@ -182,7 +188,8 @@ static int gemm_validate(const void* x, int64_t ldx, const void* w, int64_t ldw,
 // nk_gemm_bf16_argmax (bf16 y or none, plus the per-token argmax).
 static int gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
                      int64_t ldy, bool y_f32, int M, int N, int K, const nk_plan* p, void* ws,
-                     size_t ws_bytes, nk_stream_t stream, const AmaxOut* amax = nullptr);
+                     size_t ws_bytes, nk_stream_t stream, const AmaxOut* amax = nullptr,
+                     const ArIn* ar = nullptr);
 
 }  // namespace nk
 
@@ -223,7 +230,8 @@ static int nk::gemm_validate(const void* x, int64_t ldx, const void* w, int64_t 
 
 static int nk::gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
                          int64_t ldy, bool y_f32, int M, int N, int K, const nk_plan* p,
-                         void* ws, size_t ws_bytes, nk_stream_t stream, const AmaxOut* amax) {
+                         void* ws, size_t ws_bytes, nk_stream_t stream, const AmaxOut* amax,
+                         const ArIn* ar) {
     const int valid = gemm_validate(x, ldx, w, ldw, y, ldy, y_f32, M, N, K, p, amax);
     if (valid != NK_OK) return valid;
     if (amax) {
@@ -252,6 +260,11 @@ static int nk::gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw,
     a.amax_idx = nullptr;
     a.amax_best = nullptr;
     a.withhold_tile = p->kind == NK_KIND_TC ? g_withhold_tile.exchange(-1) : -1;
+    for (int r = 0; r < NK_PEER_MAX_RANKS_INTERNAL; ++r)
+        a.ar_buf[r] = ar && r < ar->world ? static_cast<uint8_t*>(ar->buf[r]) : nullptr;
+    a.ar_rank = ar ? ar->rank : 0;
+    a.ar_world = ar ? ar->world : 0;
+    a.ar_max_elems = ar ? ar->max_elems : 0;
     if (amax) {
         a.amax_keys =  // keys kAmaxKeyStride bytes apart
             reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + kAmaxOffset);

@@ -1,16 +1,9 @@
 // One-shot all-reduce of fp32 partials over NVLink peer memory (include/nk_comm.h), launched
 // with programmatic dependent launch so it starts while the GEMM that made the partial drains.
 //
-// Buffer of one rank (zeroed once, mapped into every rank of the group):
-//   [0, 4 KB)            progress counter of each CTA index (read and advanced by that CTA)
-//   [4 KB, 68 KB)        flags[2 sets][8 source ranks][1024 CTAs], u32
-//   [68 KB, ...)         slots[2 sets][world source ranks][max_elems], fp32
-// Call e (1, 2, ...) of CTA c uses set e & 1: the CTA writes its 1024-element slice of the
-// local partial into slots[set][rank] of every rank, fences at system scope, writes e into
-// flags[set][rank][c] of every rank (release), waits for flags[set][r][c] == e for all r in its
-// own buffer (acquire, bounded) and sums slots[set][0..world) in rank order. Two sets suffice:
-// a rank can only start writing call e+2 into a peer once it has seen that peer's flag for
-// call e+1, i.e. once the peer has finished call e on its stream.
+// The receive buffers and the call protocol (progress counters, two sets of flags and slots)
+// are described with their layout in nk_common.cuh; here index i is CTA i, which moves
+// elements [1024 i, 1024 i + 1024) of the partial.
 #include <string.h>
 
 #include "nk_common.cuh"
@@ -21,34 +14,13 @@ namespace nk {
 constexpr int kArThreads = 256;
 constexpr int kArElemsPerCta = kArThreads * 4;
 constexpr int kArMaxCtas = NK_PEER_MAX_ELEMS / kArElemsPerCta;  // 1024
-constexpr size_t kArEpochBytes = (size_t)kArMaxCtas * 4;
-constexpr size_t kArFlagBytes = 2ull * NK_PEER_MAX_RANKS * kArMaxCtas * 4;
-constexpr size_t kArHeader = kArEpochBytes + kArFlagBytes;
+static_assert(kArMaxCtas == kArMaxIndex, "one flag per all-reduce CTA");
+static_assert(NK_PEER_MAX_RANKS == NK_PEER_MAX_RANKS_INTERNAL, "group size");
 
 struct PeerArgs {
     uint8_t* buf[NK_PEER_MAX_RANKS];
     int rank, world, max_elems;
 };
-
-__device__ __forceinline__ unsigned* ar_flag(uint8_t* base, int set, int src, int cta) {
-    return reinterpret_cast<unsigned*>(base + kArEpochBytes) +
-           ((size_t)(set * NK_PEER_MAX_RANKS + src) * kArMaxCtas + cta);
-}
-
-__device__ __forceinline__ float* ar_slot(uint8_t* base, int set, int src, int world,
-                                          int max_elems) {
-    return reinterpret_cast<float*>(base + kArHeader) + (size_t)(set * world + src) * max_elems;
-}
-
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 __global__ void __launch_bounds__(kArThreads)
 allreduce_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out, int n,
@@ -163,6 +135,33 @@ extern "C" int nk_ipc_open(const void* handle, void** ptr) {
 extern "C" int nk_ipc_close(void* ptr) {
     if (!ptr) return NK_ERR_ARG;
     return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? NK_OK : NK_ERR_CUDA;
+}
+
+extern "C" int nk_gemm_bf16_allreduce(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                      void* y, int64_t ldy, int M, int N, int K,
+                                      const nk_plan* p, void* ws, size_t ws_bytes,
+                                      const nk_peer_group* g, nk_stream_t stream) {
+    if (!g || !y) return NK_ERR_ARG;
+    if (g->world < 2 || g->world > NK_PEER_MAX_RANKS || g->rank < 0 || g->rank >= g->world ||
+        g->max_elems < 1 || g->max_elems > NK_PEER_MAX_ELEMS)
+        return NK_ERR_ARG;
+    if (!p || p->magic != NK_PLAN_MAGIC) return NK_ERR_PLAN;
+    // the balanced tensor-core schedule (whole grid resident), token tiles of up to 64, one
+    // flag index per output tile
+    if (p->kind != NK_KIND_TC || p->split_k != 0 || p->tile_m > 64 ||
+        (int64_t)p->n_tiles * p->m_tiles > kArMaxIndex)
+        return NK_ERR_PLAN;
+    if (M < 1 || N < 1 || (int64_t)M * N > g->max_elems) return NK_ERR_SHAPE;
+    ArIn ar;
+    for (int r = 0; r < NK_PEER_MAX_RANKS; ++r) {
+        ar.buf[r] = r < g->world ? g->buf[r] : nullptr;
+        if (r < g->world && (!ar.buf[r] || ((uintptr_t)ar.buf[r] & 255u))) return NK_ERR_ARG;
+    }
+    ar.rank = g->rank;
+    ar.world = g->world;
+    ar.max_elems = g->max_elems;
+    return gemm_impl(x, ldx, w, ldw, y, ldy, false, M, N, K, p, ws, ws_bytes, stream, nullptr,
+                     &ar);
 }
 
 extern "C" int nk_allreduce_bf16(const float* x, void* out, int n, const nk_peer_group* g,

@@ -13,6 +13,9 @@
 
 namespace nk {
 
+// Largest tensor-parallel group (NK_PEER_MAX_RANKS in include/nk_comm.h).
+#define NK_PEER_MAX_RANKS_INTERNAL 8
+
 // B200 (sm_100a): 148 SMs on two dies.
 constexpr int kNumSMs = 148;
 
@@ -226,6 +229,51 @@ struct TcPartition {
     __host__ __device__ int last_cta(int t) const { return cta_of((int64_t)(t + 1) * KB - 1); }
 };
 
+// ---------------------------------------------------------------------------------------
+// Peer receive buffers of a tensor-parallel group (include/nk_comm.h). Buffer of one rank,
+// zeroed once and mapped into every rank of the group:
+//   [0, 4 KB)            progress counter per index (read and advanced by the one CTA that
+//                        owns that index in a call)
+//   [4 KB, 68 KB)        flags[2 sets][8 source ranks][1024 indices], u32
+//   [68 KB, ...)         slots[2 sets][world source ranks][max_elems], fp32
+// Call e (1, 2, ...) of index i uses set e & 1: its owner writes this rank's values into
+// slots[set][rank] of every rank, fences at system scope, writes e into flags[set][rank][i] of
+// every rank (release), waits for flags[set][r][i] == e for all r in its own buffer (acquire,
+// bounded) and sums slots[set][0..world) in rank order. Two sets suffice: a rank can only
+// start writing call e+2 into a peer once it has seen that peer's flag for call e+1, i.e. once
+// the peer has finished call e on its stream. An index is a CTA of nk_allreduce_bf16 or an
+// output tile of nk_gemm_bf16_allreduce; a group serves one of the two, as the elements an
+// index covers differ between them.
+// ---------------------------------------------------------------------------------------
+constexpr int kArMaxIndex = 1024;
+constexpr size_t kArEpochBytes = (size_t)kArMaxIndex * 4;
+constexpr size_t kArFlagBytes = 2ull * NK_PEER_MAX_RANKS_INTERNAL * kArMaxIndex * 4;
+constexpr size_t kArHeader = kArEpochBytes + kArFlagBytes;
+
+__device__ __forceinline__ unsigned* ar_counter(uint8_t* base, int index) {
+    return reinterpret_cast<unsigned*>(base) + index;
+}
+
+__device__ __forceinline__ unsigned* ar_flag(uint8_t* base, int set, int src, int index) {
+    return reinterpret_cast<unsigned*>(base + kArEpochBytes) +
+           ((size_t)(set * NK_PEER_MAX_RANKS_INTERNAL + src) * kArMaxIndex + index);
+}
+
+__device__ __forceinline__ float* ar_slot(uint8_t* base, int set, int src, int world,
+                                          int max_elems) {
+    return reinterpret_cast<float*>(base + kArHeader) + (size_t)(set * world + src) * max_elems;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Launch arguments handed from the C ABI to a kernel family.
 struct GemmArgs {
     const __nv_bfloat16* x; int64_t ldx;
@@ -248,6 +296,9 @@ struct GemmArgs {
     unsigned* amax_done;            // CTAs that have folded their rows in, zero between calls
     int64_t* amax_idx;              // [M] lowest index of each token's largest bf16 output
     __nv_bfloat16* amax_best;       // [M] that largest value, or nullptr
+    // fused all-reduce (nk_gemm_bf16_allreduce) only; ar_world == 0 otherwise
+    uint8_t* ar_buf[NK_PEER_MAX_RANKS_INTERNAL];  // every rank's receive buffer, as mapped here
+    int ar_rank, ar_world, ar_max_elems;
 };
 
 int launch_gemv(const nk_plan& p, const GemmArgs& a, cudaStream_t s);

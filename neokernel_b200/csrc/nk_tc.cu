@@ -105,6 +105,14 @@ __device__ __forceinline__ void tma_load_w(uint32_t dst, const CUtensorMap* map,
         : "memory");
 }
 
+// Prefetch one [rows x 64] tile of a tensor map into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int c0, int c1) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1)
+                 : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -210,6 +218,9 @@ __host__ __device__ constexpr uint32_t tc_idesc(int m, int n) {
 #ifndef NK_TC_SMEM_LARGE
 #define NK_TC_SMEM_LARGE (200 * 1024)  // token tiles >= 128: one CTA per SM
 #endif
+#ifndef NK_TC_L2_AHEAD
+#define NK_TC_L2_AHEAD 0  // units of weight prefetched into L2 ahead of the ring (0 = none)
+#endif
 #ifndef NK_TC_L2_PROMO
 #define NK_TC_L2_PROMO CU_TENSOR_MAP_L2_PROMOTION_L2_256B
 #endif
@@ -228,7 +239,7 @@ struct TcSmem {
     static constexpr int kPartBars = 8;                  // partial chunks in flight (finisher)
     static constexpr int kNumBars = 2 * kStages + 4 + kPartBars;  // full, empty, tfull[2], tempty[2], part
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-    static constexpr int kBytes = kMiscOff + 16;         // tmem slot, abort flag, last flag
+    static constexpr int kBytes = kMiscOff + 32;  // tmem slot, abort, last, all-reduce call, ok
     static constexpr int kAlloc = kBytes + 1024;         // slack to align the base to 1 KB
     static constexpr int kTmemCols = 2 * NT < 32 ? 32 : 2 * NT;  // two accumulators
     // 228 KB of shared memory per SM, 1 KB of it reserved per resident CTA
@@ -404,12 +415,30 @@ __device__ __forceinline__ Segment segment_at(int64_t u, int64_t u_end, int KB) 
 // warps per SM need at most 128 registers a thread (each SM sub-partition holds up to four
 // of the twelve warps), hence the cap for the token tiles that fit twice in shared memory.
 #define NK_TC_MAXNREG 128
-// AMAX: the greedy-head variant (nk_gemm_bf16_argmax) — folds every final output into the
-// tokens' (value, index) keys and may skip storing y; the plain variant compiles without it.
-template <int NT, bool AMAX>
+// Kernel variants (template MODE), each compiled only with its own code:
+//   kModePlain: y = x · Wᵀ (nk_gemm_bf16, nk_gemm_bf16_f32out, nk_gemm_bf16_static);
+//   kModeAmax:  the greedy head (nk_gemm_bf16_argmax) — folds every final output into the
+//               tokens' (value, index) keys and may skip storing y;
+//   kModeAr:    the K-split linear of a tensor-parallel group fused with its all-reduce
+//               (nk_gemm_bf16_allreduce) — each output tile's fp32 values go straight into
+//               every rank's receive buffer, and the CTA that made them adds up all ranks'
+//               values of the tile in rank order and stores y.
+constexpr int kModePlain = 0, kModeAmax = 1, kModeAr = 2;
+
+// The fused all-reduce's final value of output (m, n): this rank's fp32 value into the tile's
+// slot of every rank of the group (the sum follows once every rank has published the tile).
+__device__ __forceinline__ void ar_publish(const GemmArgs& a, int set, int m, int n, float v) {
+    const size_t off = (size_t)m * a.N + n;
+    for (int r = 0; r < a.ar_world; ++r)
+        ar_slot(a.ar_buf[r], set, a.ar_rank, a.ar_world, a.ar_max_elems)[off] = v;
+}
+
+template <int NT, int MODE>
 __global__ void __launch_bounds__(kTcThreads) __maxnreg__(NT <= 64 ? NK_TC_MAXNREG : 255)
 tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
           GemmArgs a) {
+    constexpr bool AMAX = MODE == kModeAmax;
+    constexpr bool AR = MODE == kModeAr;
     using L = TcSmem<NT>;
     constexpr int STAGES = L::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -435,6 +464,8 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
     volatile uint32_t* tmem_slot = misc;
     volatile uint32_t* abort_flag = misc + 1;
     volatile uint32_t* last_flag = misc + 2;
+    volatile uint32_t* ar_call = misc + 3;  // fused all-reduce: this tile's call number
+    volatile uint32_t* ar_ok = misc + 4;    // fused all-reduce: every rank's tile arrived
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
@@ -491,6 +522,20 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                     tma_load_2d(base + i * L::kStage + L::kA + ub * L::kBoxB, &tmap_x,
                                 bar_full + 8 * i, kb * kTcKStep + ub * kTcBox, (t / a.n_tiles) * NT);
             }
+            // Rolling L2 prefetch of the weight tiles NK_TC_L2_AHEAD units ahead of the ring:
+            // DRAM keeps that many more units in flight than the ring's stages hold, and the
+            // ring's own loads then find their tiles in L2.
+            auto prefetch_unit = [&](int i) {
+                if (NK_TC_L2_AHEAD > 0 && i < n_units) {
+                    const int64_t u = u_begin + i;
+                    const int t = (int)(u / KB);
+                    const int kb = (int)(u - (int64_t)t * KB);
+#pragma unroll
+                    for (int ub = 0; ub < kTcUK; ++ub)
+                        tma_prefetch_l2(&tmap_w, kb * kTcKStep + ub * kTcBox, (t % a.n_tiles) * kTcRows);
+                }
+            };
+            for (int i = n_pre; i < n_pre + NK_TC_L2_AHEAD; ++i) prefetch_unit(i);
             int issued = n_pre;
             for (int i = n_pre; i < n_units; ++i) {
                 const int st = i % STAGES;
@@ -511,6 +556,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                     tma_load_2d(sa + L::kA + ub * L::kBoxB, &tmap_x, bar_full + 8 * st,
                                 kb * kTcKStep + ub * kTcBox, (t / a.n_tiles) * NT);
                 ++issued;
+                prefetch_unit(i + NK_TC_L2_AHEAD);
             }
             // Drain: every stage's last load has landed and (unless the MMA issuer gave up)
             // every MMA that read it has completed before this CTA may exit.
@@ -586,6 +632,18 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             // Failure-detection tests only: this CTA keeps its partial to itself, so the tile's
             // finisher's bounded wait runs out (NK_ERR_TIMEOUT) instead of completing.
             const bool withhold = wait_mode && rank == 1 && sg.t == a.withhold_tile;
+            // Fused all-reduce: the call number of this output tile (its progress counter in
+            // this rank's receive buffer, plus one) picks the set of flags and slots.
+            unsigned ar_e = 0;
+            int ar_set = 0;
+            if constexpr (AR) {
+                if (whole || finisher) {
+                    if (ep == 0) *ar_call = *ar_counter(a.ar_buf[a.ar_rank], sg.t) + 1u;
+                    epi_bar();
+                    ar_e = *ar_call;
+                    ar_set = (int)(ar_e & 1u);
+                }
+            }
             // Rank 0 of a shared tile holds the tile's first K blocks as its last segment; the
             // other ranks (higher CTAs) hold the rest. It waits for them while its own last
             // MMAs still run and, for the decode token tile, already adds up their partials
@@ -624,7 +682,12 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                         if (c0 >= mcount) break;  // warp-uniform
                         float v[16];
                         tmem_ld16(taddr + c0, v);
-                        if (store_y && n < a.N) {
+                        if constexpr (AR) {
+                            if (n < a.N)
+#pragma unroll
+                                for (int j = 0; j < 16; ++j)
+                                    if (c0 + j < mcount) ar_publish(a, ar_set, m0 + c0 + j, n, v[j]);
+                        } else if (store_y && n < a.N) {
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
                                 if (c0 + j < mcount)
@@ -700,7 +763,13 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                             for (int j = 0; j < 16; ++j) ps[j] += sm[(i * 16 + j) * kTcRows];
 #pragma unroll
                         for (int j = 0; j < 16; ++j) v[j] += ps[j];
-                        if (store_y && arrived && n < a.N) {
+                        if constexpr (AR) {
+                            if (arrived && n < a.N)
+#pragma unroll
+                                for (int j = 0; j < 16; ++j)
+                                    if (16 * k + j < mcount)
+                                        ar_publish(a, ar_set, m0 + 16 * k + j, n, v[j]);
+                        } else if (store_y && arrived && n < a.N) {
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
                                 if (16 * k + j < mcount)
@@ -732,7 +801,12 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                         tmem_ld16(taddr + c0, v);
 #pragma unroll
                         for (int j = 0; j < 16; ++j) v[j] += psum[j];
-                        if (store_y && got && n < a.N) {
+                        if constexpr (AR) {
+                            if (got && n < a.N)
+#pragma unroll
+                                for (int j = 0; j < 16; ++j)
+                                    if (c0 + j < mcount) ar_publish(a, ar_set, m0 + c0 + j, n, v[j]);
+                        } else if (store_y && got && n < a.N) {
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
                                 if (c0 + j < mcount)
@@ -785,6 +859,43 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                     if (ep == 0) a.tickets[sg.t] = 0u;  // re-armed for the next launch
                 }
                 epi_bar();  // last_flag is rewritten by the next partial segment
+            }
+            if constexpr (AR) {
+                if (whole || finisher) {
+                    // This rank's values of the tile are in every rank's slot: publish the call
+                    // number to every rank, wait (bounded) for every rank's, and store the sum of
+                    // the ranks' values in rank order, rounded once to bf16.
+                    uint8_t* own = a.ar_buf[a.ar_rank];
+                    __threadfence_system();  // this thread's slot stores, before the flags
+                    if (ep == 0) *ar_ok = 1u;
+                    epi_bar();
+                    if (ep < a.ar_world)
+                        st_release_sys(ar_flag(a.ar_buf[ep], ar_set, a.ar_rank, sg.t), ar_e);
+                    if (ep < a.ar_world) {
+                        const unsigned* f = ar_flag(own, ar_set, ep, sg.t);
+                        const uint64_t t0 = global_ns();
+                        while (ld_acquire_sys(f) != ar_e) {
+                            if (global_ns() - t0 > 2000000000ull) {
+                                atomicExch(&g_error, NK_ERR_TIMEOUT);
+                                *ar_ok = 0u;
+                                break;
+                            }
+                            __nanosleep(64);
+                        }
+                    }
+                    epi_bar();
+                    if (*ar_ok && n < a.N) {
+                        for (int j = 0; j < mcount; ++j) {
+                            const size_t off = (size_t)(m0 + j) * a.N + n;
+                            float acc =
+                                __ldcg(ar_slot(own, ar_set, 0, a.ar_world, a.ar_max_elems) + off);
+                            for (int r = 1; r < a.ar_world; ++r)
+                                acc += __ldcg(ar_slot(own, ar_set, r, a.ar_world, a.ar_max_elems) + off);
+                            a.y[(int64_t)(m0 + j) * a.ldy + n] = __float2bfloat16_rn(acc);
+                        }
+                    }
+                    if (ep == 0) *ar_counter(own, sg.t) = ar_e;
+                }
             }
         }
         if constexpr (AMAX) {
@@ -889,18 +1000,18 @@ int tc_ctas_per_sm(int nt) {
     }
 }
 
-// CTAs of tc_kernel<NT, AMAX> that fit on one SM at once. The runtime's occupancy query answers 1
+// CTAs of tc_kernel<NT, MODE> that fit on one SM at once. The runtime's occupancy query answers 1
 // for every kernel that executes tcgen05.alloc (on B200 even for a 12-register kernel), but
 // the block scheduler places such CTAs by registers, shared memory and threads: 296 CTAs
 // that each hold 32 TMEM columns run on 148 SMs as one wave, two overlapping on every SM.
 // So the count is made here from those limits, plus the 512 TMEM columns of an SM (so no
 // CTA blocks in tcgen05.alloc), and capped at the per-SM count the stage budget assumes.
-template <int NT, bool AMAX>
+template <int NT, int MODE>
 static int tc_resident_per_sm(int dev) {
     using L = TcSmem<NT>;
     cudaFuncAttributes fa;
     int smem_sm = 0, reserved = 0, regs_sm = 0, thr_sm = 0;
-    if (cudaFuncGetAttributes(&fa, tc_kernel<NT, AMAX>) != cudaSuccess ||
+    if (cudaFuncGetAttributes(&fa, tc_kernel<NT, MODE>) != cudaSuccess ||
         cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) !=
             cudaSuccess ||
         cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) !=
@@ -923,7 +1034,7 @@ static int tc_resident_per_sm(int dev) {
     return n;
 }
 
-template <int NT, bool AMAX>
+template <int NT, int MODE>
 static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
                        const CUtensorMap& mx, cudaStream_t s) {
     using L = TcSmem<NT>;
@@ -932,15 +1043,15 @@ static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
     if (cudaGetDevice(&dev) != cudaSuccess) return NK_ERR_CUDA;
     if (dev < 0 || dev >= 64) return NK_ERR_DEVICE;
     if (resident[dev] == 0) {
-        if (cudaFuncSetAttribute(tc_kernel<NT, AMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(tc_kernel<NT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  L::kAlloc) != cudaSuccess ||
-            cudaFuncSetAttribute(tc_kernel<NT, AMAX>, cudaFuncAttributePreferredSharedMemoryCarveout,
+            cudaFuncSetAttribute(tc_kernel<NT, MODE>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return NK_ERR_CUDA;
         int sms = 0;
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
             return NK_ERR_CUDA;
-        const int per_sm = tc_resident_per_sm<NT, AMAX>(dev);
+        const int per_sm = tc_resident_per_sm<NT, MODE>(dev);
         if (per_sm < 1) return NK_ERR_CUDA;
         resident[dev] = per_sm * sms;
     }
@@ -960,6 +1071,8 @@ static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
         P.G = (int)G;
     }
     a.coresident = P.G <= resident[dev] ? 1 : 0;
+    // The fused all-reduce finishes every tile in the waiting protocol: the whole grid resident.
+    if (MODE == kModeAr && !a.coresident) return NK_ERR_PLAN;
     const int grid = P.G;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
@@ -971,7 +1084,7 @@ static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = NK_PDL ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, tc_kernel<NT, AMAX>, mw, mx, a) == cudaSuccess ? NK_OK
+    return cudaLaunchKernelEx(&cfg, tc_kernel<NT, MODE>, mw, mx, a) == cudaSuccess ? NK_OK
                                                                                       : NK_ERR_CUDA;
 }
 
@@ -992,19 +1105,22 @@ int launch_tc(const nk_plan& p, const GemmArgs& in, cudaStream_t s) {
     CUtensorMap mw, mx;
     if (make_map(&mw, a.w, a.N, a.K, a.ldw, kTcRows) != NK_OK) return NK_ERR_ALIGN;
     if (make_map(&mx, a.x, a.M, a.K, a.ldx, nt) != NK_OK) return NK_ERR_ALIGN;
-    const bool amax = a.amax_keys != nullptr;
-    switch (nt) {
-        case 16: return amax ? launch_tc_t<16, true>(p, a, mw, mx, s)
-                       : launch_tc_t<16, false>(p, a, mw, mx, s);
-        case 32: return amax ? launch_tc_t<32, true>(p, a, mw, mx, s)
-                       : launch_tc_t<32, false>(p, a, mw, mx, s);
-        case 64: return amax ? launch_tc_t<64, true>(p, a, mw, mx, s)
-                       : launch_tc_t<64, false>(p, a, mw, mx, s);
-        case 128: return amax ? launch_tc_t<128, true>(p, a, mw, mx, s)
-                       : launch_tc_t<128, false>(p, a, mw, mx, s);
-        case 256: return amax ? launch_tc_t<256, true>(p, a, mw, mx, s)
-                       : launch_tc_t<256, false>(p, a, mw, mx, s);
-        default: return NK_ERR_PLAN;
+    const int mode = a.amax_keys ? kModeAmax : (a.ar_world > 0 ? kModeAr : kModePlain);
+    switch (nt * 4 + mode) {
+        case 16 * 4 + kModePlain: return launch_tc_t<16, kModePlain>(p, a, mw, mx, s);
+        case 16 * 4 + kModeAmax: return launch_tc_t<16, kModeAmax>(p, a, mw, mx, s);
+        case 16 * 4 + kModeAr: return launch_tc_t<16, kModeAr>(p, a, mw, mx, s);
+        case 32 * 4 + kModePlain: return launch_tc_t<32, kModePlain>(p, a, mw, mx, s);
+        case 32 * 4 + kModeAmax: return launch_tc_t<32, kModeAmax>(p, a, mw, mx, s);
+        case 32 * 4 + kModeAr: return launch_tc_t<32, kModeAr>(p, a, mw, mx, s);
+        case 64 * 4 + kModePlain: return launch_tc_t<64, kModePlain>(p, a, mw, mx, s);
+        case 64 * 4 + kModeAmax: return launch_tc_t<64, kModeAmax>(p, a, mw, mx, s);
+        case 64 * 4 + kModeAr: return launch_tc_t<64, kModeAr>(p, a, mw, mx, s);
+        case 128 * 4 + kModePlain: return launch_tc_t<128, kModePlain>(p, a, mw, mx, s);
+        case 128 * 4 + kModeAmax: return launch_tc_t<128, kModeAmax>(p, a, mw, mx, s);
+        case 256 * 4 + kModePlain: return launch_tc_t<256, kModePlain>(p, a, mw, mx, s);
+        case 256 * 4 + kModeAmax: return launch_tc_t<256, kModeAmax>(p, a, mw, mx, s);
+        default: return NK_ERR_PLAN;  // the fused all-reduce takes token tiles of up to 64
     }
 }
 

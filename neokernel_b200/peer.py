@@ -5,8 +5,11 @@ other rank of the process group with CUDA IPC (the handles travel over the proce
 ``allreduce_bf16(x, out)`` launches ``nk_allreduce_bf16``: out = bf16(x_0 + ... + x_{T-1}),
 ranks added in rank order, on the current stream, capturable in a CUDA graph. It stands in for
 ``dist.all_reduce`` followed by the bf16 copy in the tensor-parallel hooks (neokernel_b200/tp.py)
-for the linears split along K (engine/kernels/decode.py:58,66). Every rank must make the same
-sequence of calls.
+for the linears split along K (engine/kernels/decode.py:58,66). ``mm_allreduce(a, b, out)``
+goes one step further and launches ``nk_gemm_bf16_allreduce``: the K-slice linear itself,
+whose kernel stores each output tile's fp32 values straight into every rank's buffer and
+adds up the ranks' values of the tile. A group serves one of the two kinds of call. Every
+rank must make the same sequence of calls.
 """
 
 from __future__ import annotations
@@ -75,6 +78,39 @@ class PeerGroup:
         st = self._L.nk_allreduce_bf16(x.data_ptr(), out.data_ptr(), x.numel(), self._ref, s)
         if st != _lib.NK_OK:
             _raise(st, "nk_allreduce_bf16")
+        return out
+
+    def mm_allreduce(self, a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor,
+                     plan=None) -> torch.Tensor:
+        """out = bf16(sum over ranks of a_r @ b_r), ranks added in rank order: this rank's K
+        slice of a tensor-parallel linear fused with its all-reduce in one launch
+        (``nk_gemm_bf16_allreduce``). a: bf16 [M, K_r]; b = W_r.t() of a row-major [N, K_r]
+        weight slice; out: bf16 [M, N] contiguous. The group must be made for at least M * N
+        elements and serve no ``allreduce_bf16`` calls; every rank makes the same calls."""
+        from . import gemm
+        gemm._check_tensor(a, "a")
+        gemm._check_tensor(b, "b")
+        gemm._check_tensor(out, "out")
+        M, K = a.shape
+        K2, N = b.shape
+        if K2 != K or tuple(out.shape) != (M, N):
+            raise ValueError(f"mm_allreduce: a [{M}, {K}], b [{K2}, {N}], out {tuple(out.shape)}")
+        if a.stride(1) != 1 or b.stride(0) != 1 or not out.is_contiguous():
+            raise ValueError("mm_allreduce: a row-major, b = W.t() of a row-major weight, "
+                             "out contiguous")
+        if M * N > self.c.max_elems:
+            raise ValueError(f"mm_allreduce: {M} x {N} outputs exceed the group's "
+                             f"{self.c.max_elems} elements")
+        plan = plan or gemm.plan_for(M, N, K)
+        dev = a.device
+        stream = torch.cuda.current_stream(dev)
+        ws = gemm.workspace(max(plan.ws_bytes, 1), dev, stream) if plan.ws_bytes else None
+        st = self._L.nk_gemm_bf16_allreduce(
+            a.data_ptr(), a.stride(0) if M > 1 else K, b.data_ptr(), b.stride(1) if N > 1 else K,
+            out.data_ptr(), N, M, N, K, plan._ref, ws.data_ptr() if ws is not None else None,
+            ws.numel() if ws is not None else 0, self._ref, stream.cuda_stream)
+        if st != _lib.NK_OK:
+            _raise(st, f"nk_gemm_bf16_allreduce(M={M}, N={N}, K={K})")
         return out
 
     def close(self):

@@ -9,11 +9,12 @@ shards the decode linears where their weights shard naturally:
 * gate_up (decode.py:64) is split by output column with the gate and up slices paired, so
   bf16(silu(gate)) * up is local;
 * o_proj (decode.py:58) and down (decode.py:66) are split along K: each rank computes an
-  unrounded fp32 partial (``mm_f32``), the partials are summed across ranks and the sum is
-  rounded to bf16 once — the single-GPU rounding. On GPUs the sum is ``nk_allreduce_bf16``
-  (neokernel_b200/peer.py): one launch per rank that writes its partial into every rank's
-  buffer over NVLink and adds the ranks in rank order; ``collective="nccl"`` uses NCCL's
-  all-reduce instead (and CPU process groups always use ``dist.all_reduce``);
+  unrounded fp32 partial, the partials are summed across ranks and the sum is rounded to bf16
+  once — the single-GPU rounding. On GPUs the product fuses the linear with that sum
+  (``nk_gemm_bf16_allreduce``, neokernel_b200/peer.py): one launch per rank whose output tiles
+  go straight into every rank's buffer over NVLink and are added up in rank order there.
+  ``collective="peer"`` keeps the two launches (``mm_f32``, then ``nk_allreduce_bf16``),
+  ``collective="nccl"`` uses NCCL's all-reduce (as CPU process groups always do);
 * lm_head (engine.py:114) is split by vocabulary row: each rank takes its local max and its
   lowest index — on GPUs in the lm_head launch itself (``mm_argmax``, the fused greedy head),
   so the [B, vocab / T] logits are not stored — and an all-gather of (value, index) picks the
@@ -97,7 +98,7 @@ class TPWeights:
         self.vocab_offset = rank * vl
 
 
-PEER_MAX_AUTO = 1 << 16  # fp32 elements up to which "auto" sums partials over peer memory
+FUSED_MAX_M = 64  # batches up to which "auto" fuses the K-split linears with their all-reduce
 
 
 def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None, collective="auto",
@@ -106,17 +107,17 @@ def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None, collectiv
 
     ``linear_f32(a, b, out)`` computes an unrounded fp32 partial (default:
     ``neokernel_b200.mm_f32``); ``linear(a, b, out)`` the bf16 lm_head shard (default:
-    ``neokernel_b200.mm``). ``collective`` sums the partials of the K-split linears: "peer"
-    (``nk_allreduce_bf16`` over NVLink peer memory), "nccl" (``dist.all_reduce``, then the bf16
-    copy) or "auto": peer on a CUDA process group of 2+ ranks for partials of up to
-    ``PEER_MAX_AUTO`` elements, else all_reduce (measured on B200, Qwen3-32B TP=2: the peer
-    sum is ahead at batch 1 and behind NCCL at batch 32). ``fused_head`` (CUDA states only)
+    ``neokernel_b200.mm``). ``collective`` sums the partials of the K-split linears: "fused"
+    (the linear and the sum in one launch, ``PeerGroup.mm_allreduce``), "peer" (``mm_f32`` then
+    ``nk_allreduce_bf16`` over NVLink peer memory), "nccl" (``mm_f32``, ``dist.all_reduce``,
+    then the bf16 copy) or "auto": fused on a CUDA process group of 2+ ranks for batches of up
+    to ``FUSED_MAX_M``, else all_reduce. ``fused_head`` (CUDA states only)
     takes each rank's (max, lowest index) from the lm_head launch (``neokernel_b200.mm_argmax``)
     instead of storing the logits and reducing them; ``state.logits`` is then left untouched.
     Buffers are allocated here, once per state, so the hooks are capture-safe.
     """
-    if collective not in ("auto", "peer", "nccl"):
-        raise ValueError(f"collective must be auto, peer or nccl, not {collective!r}")
+    if collective not in ("auto", "fused", "peer", "nccl"):
+        raise ValueError(f"collective must be auto, fused, peer or nccl, not {collective!r}")
     if linear_f32 is None or linear is None:
         import neokernel_b200 as nk
         linear_f32 = linear_f32 or nk.mm_f32
@@ -126,11 +127,12 @@ def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None, collectiv
     def make(st: qwen3.DecodeState):
         B, H = st.batch, w.dims.hidden
         dev = st.x.device
-        use_peer = world > 1 and (collective == "peer" or (
-            collective == "auto" and dev.type == "cuda" and dist.get_backend(group) == "nccl"
-            and B * H <= PEER_MAX_AUTO))
+        gpu_group = world > 1 and dev.type == "cuda" and dist.get_backend(group) == "nccl"
+        use_fused = world > 1 and (collective == "fused" or (
+            collective == "auto" and gpu_group and B <= FUSED_MAX_M))
+        use_peer = not use_fused and world > 1 and collective == "peer"
         peer = None
-        if use_peer:
+        if use_fused or use_peer:
             from .peer import PeerGroup
             peer = PeerGroup(B * H, group=group, device=dev)
         partial = torch.empty(B, H, device=dev, dtype=torch.float32)
@@ -142,6 +144,9 @@ def make_hooks(w: TPWeights, group=None, linear_f32=None, linear=None, collectiv
         all_idx = torch.empty(world * B, device=dev, dtype=torch.int64)
 
         def row_linear(a, b, out):
+            if use_fused:  # the K-slice linear and the rank-order sum in one launch
+                peer.mm_allreduce(a, b, out=out)
+                return
             linear_f32(a, b, out=partial)
             if peer is not None:
                 peer.allreduce_bf16(partial, out)  # rank-order sum, one rounding to bf16

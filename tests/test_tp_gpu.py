@@ -1,6 +1,7 @@
 """Tensor-parallel decode on 2+ GPUs, CUDA-graph captured, against the single-GPU model of the
-same seed on every rank, with the K-split partials summed by the peer-memory all-reduce
-(nk_allreduce_bf16) and by NCCL. Skipped with fewer than two GPUs."""
+same seed on every rank, with the K-split partials summed inside the linear's own launch
+(nk_gemm_bf16_allreduce), by the peer-memory all-reduce (nk_allreduce_bf16) and by NCCL.
+Skipped with fewer than two GPUs."""
 
 import multiprocessing as mp
 import os
@@ -74,7 +75,7 @@ def _worker(rank, world, port, q, collective):
 
 
 @pytest.mark.skipif(N_GPUS < 2, reason="needs two or more GPUs")
-@pytest.mark.parametrize("collective", ("peer", "nccl"))
+@pytest.mark.parametrize("collective", ("fused", "peer", "nccl"))
 def test_tp_decode_matches_single_gpu_model(collective):
     world = 4 if N_GPUS >= 4 else 2
     ctx = mp.get_context("spawn")
