@@ -37,6 +37,28 @@ NK_API int nk_qk_norm_rope_cache_bf16(const void* qkv, int64_t ld_qkv, const voi
                                       int64_t cache_batch_stride, int64_t cache_head_stride,
                                       int64_t cache_seq_stride, float eps, nk_stream_t stream);
 
+/* The QKV linear and its consumer in one launch: qkv = x · Wqkvᵀ (nk_gemm_bf16's arithmetic,
+ * W the packed [(q_heads + 2 kv_heads) * 128, K] weight) is never stored; each 128-row output
+ * tile is one head, and the CTA that finishes a tile applies to it exactly what
+ * nk_qk_norm_rope_cache_bf16 applies to the stored bf16 qkv row (same roundings, same sum
+ * order, so the same bits): query and key heads RMSNorm + RoPE at *position into q_out and
+ * the key cache, value heads into the value cache. Replaces torch.mm(norm, w.qkv, out=qkv)
+ * followed by qk_rope_cache_out (engine/kernels/decode.py:54-55,
+ * engine/kernels/elementwise.py:63-78); the reference's handoff names this "producer +
+ * consumer" fusion as the next step (docs/NEXT_MODEL_HANDOFF.md:93-97).
+ *   x: [M, K], row stride ldx; w, ldw, plan, ws, ws_bytes as nk_gemm_bf16, with a
+ *   tensor-core plan of decode token tiles (M_max <= 16) in the balanced schedule (split_k 0;
+ *   else NK_ERR_PLAN). Other arguments as nk_qk_norm_rope_cache_bf16 (head_dim 128; batch = M).
+ *   A *position outside [0, capacity) writes nothing to q_out or the caches and sets the
+ *   device error word to NK_ERR_RANGE. */
+NK_API int nk_gemm_bf16_qkv_rope_cache(
+    const void* x, int64_t ldx, const void* w, int64_t ldw, int M, int N, int K,
+    const nk_plan* plan, void* ws, size_t ws_bytes, const void* q_norm, const void* k_norm,
+    const void* cos_table, const void* sin_table, const int64_t* position, void* q_out,
+    void* k_cache, void* v_cache, int q_heads, int kv_heads, int capacity,
+    int64_t cache_batch_stride, int64_t cache_head_stride, int64_t cache_seq_stride, float eps,
+    nk_stream_t stream);
+
 /* Workspace bytes of nk_attention_decode_bf16 (fp32 split partials and their max/sum). */
 NK_API size_t nk_attention_ws_bytes(int batch, int q_heads, int capacity);
 

@@ -41,7 +41,7 @@ EXPORTS = ("nk_plan_make", "nk_ws_bytes", "nk_ws_init", "nk_gemm_bf16", "nk_devi
            "nk_attention_decode_bf16", "nk_silu_mul_bf16", "nk_peer_buffer_bytes", "nk_peer_alloc",
            "nk_peer_free", "nk_ipc_handle", "nk_ipc_open", "nk_ipc_close", "nk_allreduce_bf16",
            "nk_gemm_argmax_ws_bytes", "nk_gemm_bf16_argmax", "nk_test_withhold_partial",
-           "nk_gemm_bf16_allreduce")
+           "nk_gemm_bf16_allreduce", "nk_gemm_bf16_qkv_rope_cache")
 
 
 NK_PEER_MAX_RANKS = 8
@@ -127,6 +127,11 @@ def load() -> ctypes.CDLL:
     L.nk_qk_norm_rope_cache_bf16.argtypes = [vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32,
                                              i32, i32, i32, i64, i64, i64, f32, vp]
     L.nk_qk_norm_rope_cache_bf16.restype = i32
+    L.nk_gemm_bf16_qkv_rope_cache.argtypes = [vp, i64, vp, i64, i32, i32, i32,
+                                              ctypes.POINTER(NkPlan), vp, ctypes.c_size_t,
+                                              vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32,
+                                              i64, i64, i64, f32, vp]
+    L.nk_gemm_bf16_qkv_rope_cache.restype = i32
     L.nk_attention_ws_bytes.argtypes = [i32, i32, i32]
     L.nk_attention_ws_bytes.restype = ctypes.c_size_t
     L.nk_attention_decode_bf16.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i64, i64,

@@ -172,6 +172,16 @@ struct AmaxOut {
     void* best;
 };
 
+// The consumer of the fused QKV epilogue (nk_gemm_bf16_qkv_rope_cache), validated.
+struct QkvIn {
+    const void *q_norm, *k_norm, *cos_t, *sin_t;
+    const int64_t* position;
+    void *q_out, *k_cache, *v_cache;
+    int hq, hkv, capacity;
+    int64_t cb, ch, cs;
+    float eps;
+};
+
 // The tensor-parallel group of the fused all-reduce (nk_gemm_bf16_allreduce), validated.
 struct ArIn {
     void* buf[NK_PEER_MAX_RANKS_INTERNAL];
@@ -182,14 +192,14 @@ struct ArIn {
 // (plan, shape, pointers, alignment). Returns NK_OK or the NK_ERR_* the entry point reports.
 static int gemm_validate(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* y,
                          int64_t ldy, bool y_f32, int M, int N, int K, const nk_plan* p,
-                         const AmaxOut* amax);
+                         const AmaxOut* amax, bool y_optional = false);
 
 // Shared body of nk_gemm_bf16 (bf16 y), nk_gemm_bf16_f32out (fp32 y) and
 // nk_gemm_bf16_argmax (bf16 y or none, plus the per-token argmax).
 static int gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
                      int64_t ldy, bool y_f32, int M, int N, int K, const nk_plan* p, void* ws,
                      size_t ws_bytes, nk_stream_t stream, const AmaxOut* amax = nullptr,
-                     const ArIn* ar = nullptr);
+                     const ArIn* ar = nullptr, const QkvIn* qk = nullptr);
 
 }  // namespace nk
 
@@ -207,11 +217,11 @@ extern "C" int nk_gemm_bf16_f32out(const void* x, int64_t ldx, const void* w, in
 
 static int nk::gemm_validate(const void* x, int64_t ldx, const void* w, int64_t ldw,
                              const void* y, int64_t ldy, bool y_f32, int M, int N, int K,
-                             const nk_plan* p, const AmaxOut* amax) {
+                             const nk_plan* p, const AmaxOut* amax, bool y_optional) {
     if (!p || p->magic != NK_PLAN_MAGIC) return NK_ERR_PLAN;
     if (p->N != N || p->K != K) return NK_ERR_PLAN;
     if (M < 1 || M > p->M_max) return NK_ERR_SHAPE;
-    if (!x || !w || (!y && !amax)) return NK_ERR_ARG;
+    if (!x || !w || (!y && !amax && !y_optional)) return NK_ERR_ARG;
     if (ldx < K || ldw < K || (y && ldy < N)) return NK_ERR_SHAPE;
     if (amax) {
         if (p->kind != NK_KIND_TC) return NK_ERR_PLAN;  // the tensor-core family only
@@ -231,8 +241,8 @@ static int nk::gemm_validate(const void* x, int64_t ldx, const void* w, int64_t 
 static int nk::gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
                          int64_t ldy, bool y_f32, int M, int N, int K, const nk_plan* p,
                          void* ws, size_t ws_bytes, nk_stream_t stream, const AmaxOut* amax,
-                         const ArIn* ar) {
-    const int valid = gemm_validate(x, ldx, w, ldw, y, ldy, y_f32, M, N, K, p, amax);
+                         const ArIn* ar, const QkvIn* qk) {
+    const int valid = gemm_validate(x, ldx, w, ldw, y, ldy, y_f32, M, N, K, p, amax, qk != nullptr);
     if (valid != NK_OK) return valid;
     if (amax) {
         if (!ws || ws_bytes < amax_ws_bytes(*p)) return NK_ERR_WORKSPACE;
@@ -265,6 +275,21 @@ static int nk::gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw,
     a.ar_rank = ar ? ar->rank : 0;
     a.ar_world = ar ? ar->world : 0;
     a.ar_max_elems = ar ? ar->max_elems : 0;
+    a.qk_qnorm = qk ? static_cast<const __nv_bfloat16*>(qk->q_norm) : nullptr;
+    a.qk_knorm = qk ? static_cast<const __nv_bfloat16*>(qk->k_norm) : nullptr;
+    a.qk_cos = qk ? static_cast<const __nv_bfloat16*>(qk->cos_t) : nullptr;
+    a.qk_sin = qk ? static_cast<const __nv_bfloat16*>(qk->sin_t) : nullptr;
+    a.qk_pos = qk ? qk->position : nullptr;
+    a.qk_q = qk ? static_cast<__nv_bfloat16*>(qk->q_out) : nullptr;
+    a.qk_k = qk ? static_cast<__nv_bfloat16*>(qk->k_cache) : nullptr;
+    a.qk_v = qk ? static_cast<__nv_bfloat16*>(qk->v_cache) : nullptr;
+    a.qk_hq = qk ? qk->hq : 0;
+    a.qk_hkv = qk ? qk->hkv : 0;
+    a.qk_cap = qk ? qk->capacity : 0;
+    a.qk_cb = qk ? qk->cb : 0;
+    a.qk_ch = qk ? qk->ch : 0;
+    a.qk_cs = qk ? qk->cs : 0;
+    a.qk_eps = qk ? qk->eps : 0.f;
     if (amax) {
         a.amax_keys =  // keys kAmaxKeyStride bytes apart
             reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + kAmaxOffset);

@@ -296,6 +296,19 @@ struct GemmArgs {
     unsigned* amax_done;            // CTAs that have folded their rows in, zero between calls
     int64_t* amax_idx;              // [M] lowest index of each token's largest bf16 output
     __nv_bfloat16* amax_best;       // [M] that largest value, or nullptr
+    // fused q/k-norm + RoPE + KV-cache epilogue (nk_gemm_bf16_qkv_rope_cache) only; qk_q is
+    // nullptr otherwise
+    const __nv_bfloat16* qk_qnorm;  // [128] query-head RMSNorm gain
+    const __nv_bfloat16* qk_knorm;  // [128] key-head RMSNorm gain
+    const __nv_bfloat16* qk_cos;    // [capacity, 128] rotary tables
+    const __nv_bfloat16* qk_sin;
+    const int64_t* qk_pos;          // device-side decode position
+    __nv_bfloat16* qk_q;            // [M, Hq * 128] roped, normalised queries
+    __nv_bfloat16* qk_k;            // key cache, element (b, h, p, d) at b*cb + h*ch + p*cs + d
+    __nv_bfloat16* qk_v;            // value cache, same strides
+    int qk_hq, qk_hkv, qk_cap;
+    int64_t qk_cb, qk_ch, qk_cs;
+    float qk_eps;
     // fused all-reduce (nk_gemm_bf16_allreduce) only; ar_world == 0 otherwise
     uint8_t* ar_buf[NK_PEER_MAX_RANKS_INTERNAL];  // every rank's receive buffer, as mapped here
     int ar_rank, ar_world, ar_max_elems;

@@ -665,3 +665,45 @@ extern "C" int nk_silu_mul_bf16(const void* gate_up, void* out, int rows, int in
                            static_cast<const __nv_bfloat16*>(gate_up),
                            static_cast<__nv_bfloat16*>(out), rows, intermediate);
 }
+
+extern "C" int nk_gemm_bf16_qkv_rope_cache(
+    const void* x, int64_t ldx, const void* w, int64_t ldw, int M, int N, int K,
+    const nk_plan* p, void* ws, size_t ws_bytes, const void* q_norm, const void* k_norm,
+    const void* cos_table, const void* sin_table, const int64_t* position, void* q_out,
+    void* k_cache, void* v_cache, int q_heads, int kv_heads, int capacity,
+    int64_t cache_batch_stride, int64_t cache_head_stride, int64_t cache_seq_stride, float eps,
+    nk_stream_t stream) {
+    if (!q_norm || !k_norm || !cos_table || !sin_table || !position || !q_out || !k_cache ||
+        !v_cache)
+        return NK_ERR_ARG;
+    if (q_heads < 1 || kv_heads < 1 || capacity < 1 || !(eps > 0.f) ||
+        cache_seq_stride < kHeadDim)
+        return NK_ERR_SHAPE;
+    if ((int64_t)N != (int64_t)(q_heads + 2 * kv_heads) * kHeadDim) return NK_ERR_SHAPE;
+    if (!p || p->magic != NK_PLAN_MAGIC) return NK_ERR_PLAN;
+    // decode token tiles in the balanced schedule (whole grid resident)
+    if (p->kind != NK_KIND_TC || p->split_k != 0 || p->tile_m != 16) return NK_ERR_PLAN;
+    if (((uintptr_t)q_out | (uintptr_t)k_cache | (uintptr_t)v_cache | (uintptr_t)q_norm |
+         (uintptr_t)k_norm | (uintptr_t)cos_table | (uintptr_t)sin_table) & 1u)
+        return NK_ERR_ALIGN;
+    if (((uintptr_t)position & 7u) != 0) return NK_ERR_ALIGN;
+    QkvIn qk;
+    qk.q_norm = q_norm;
+    qk.k_norm = k_norm;
+    qk.cos_t = cos_table;
+    qk.sin_t = sin_table;
+    qk.position = position;
+    qk.q_out = q_out;
+    qk.k_cache = k_cache;
+    qk.v_cache = v_cache;
+    qk.hq = q_heads;
+    qk.hkv = kv_heads;
+    qk.capacity = capacity;
+    qk.cb = cache_batch_stride;
+    qk.ch = cache_head_stride;
+    qk.cs = cache_seq_stride;
+    qk.eps = eps;
+    return gemm_impl(x, ldx, w, ldw, nullptr, N, false, M, N, K, p, ws, ws_bytes, stream, nullptr,
+                     nullptr, &qk);
+}
+

@@ -225,6 +225,11 @@ __host__ __device__ constexpr uint32_t tc_idesc(int m, int n) {
 #define NK_TC_L2_PROMO CU_TENSOR_MAP_L2_PROMOTION_L2_256B
 #endif
 
+// Shared memory of the fused QKV epilogue (kModeQkv, below): per column, the four warps' sums of
+// squares and the normalised head (for the RoPE partner element), double-buffered by column
+// parity.
+constexpr int kQkvSmemBytes = 2 * (4 + 128) * 4;
+
 template <int NT>
 struct TcSmem {
     static constexpr int kBoxA = kTcRows * kTcBox * 2;  // 16 KB: 128 weight rows x 128 B
@@ -239,7 +244,8 @@ struct TcSmem {
     static constexpr int kPartBars = 8;                  // partial chunks in flight (finisher)
     static constexpr int kNumBars = 2 * kStages + 4 + kPartBars;  // full, empty, tfull[2], tempty[2], part
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-    static constexpr int kBytes = kMiscOff + 32;  // tmem slot, abort, last, all-reduce call, ok
+    // tmem slot, abort, last, all-reduce call, ok; then the fused QKV epilogue's buffers
+    static constexpr int kBytes = kMiscOff + 32 + kQkvSmemBytes;
     static constexpr int kAlloc = kBytes + 1024;         // slack to align the base to 1 KB
     static constexpr int kTmemCols = 2 * NT < 32 ? 32 : 2 * NT;  // two accumulators
     // 228 KB of shared memory per SM, 1 KB of it reserved per resident CTA
@@ -423,7 +429,72 @@ __device__ __forceinline__ Segment segment_at(int64_t u, int64_t u_end, int KB) 
 //               (nk_gemm_bf16_allreduce) — each output tile's fp32 values go straight into
 //               every rank's receive buffer, and the CTA that made them adds up all ranks'
 //               values of the tile in rank order and stores y.
-constexpr int kModePlain = 0, kModeAmax = 1, kModeAr = 2;
+//   kModeQkv:   the QKV linear fused with its consumer (nk_gemm_bf16_qkv_rope_cache) — each
+//               output tile is one 128-wide head; the CTA that finishes it applies the
+//               per-head RMSNorm and RoPE of query and key heads and writes queries, keys
+//               and values where the attention reads them (decode token tiles only).
+constexpr int kModePlain = 0, kModeAmax = 1, kModeAr = 2, kModeQkv = 3;
+
+// The kModeQkv epilogue for `cols` token columns of one head tile (values v, tokens b0 + j):
+// exactly nk_qk_norm_rope_cache_bf16 (nk_decode.cu) applied to the bf16-rounded outputs, with
+// the same sum-of-squares order. Every epilogue thread calls it for the same columns (it holds
+// CTA-wide barriers); `live` only gates the stores.
+__device__ __forceinline__ void qkv_rope_chunk(const GemmArgs& a, const float (&v)[16], int cols,
+                                               int b0, int head, int d, int quarter, int lane,
+                                               bool live, float* qsm, int& parity) {
+    const int hq = a.qk_hq, hkv = a.qk_hkv;
+    const int64_t pos = *a.qk_pos;
+    const bool pos_ok = pos >= 0 && pos < a.qk_cap;
+    if (!pos_ok && head == 0 && d == 0 && b0 == 0) atomicExch(&g_error, NK_ERR_RANGE);
+    live = live && pos_ok;
+    const bool is_q = head < hq;
+    const bool is_v = head >= hq + hkv;  // value heads follow the keys
+    float wgt = 0.f, c = 0.f, sn = 0.f;
+    if (!is_v) {
+        wgt = __bfloat162float(is_q ? a.qk_qnorm[d] : a.qk_knorm[d]);
+        const int64_t p = pos_ok ? pos : 0;
+        c = __bfloat162float(a.qk_cos[p * 128 + d]);
+        sn = __bfloat162float(a.qk_sin[p * 128 + d]);
+    }
+#pragma unroll 1
+    for (int j = 0; j < cols; ++j) {
+        float x = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            if (i == j) x = v[i];
+        x = __bfloat162float(__float2bfloat16_rn(x));  // the linear's bf16 output
+        const int b = b0 + j;
+        if (is_v) {
+            const int kh = head - hq - hkv;
+            if (live) a.qk_v[(int64_t)b * a.qk_cb + (int64_t)kh * a.qk_ch + pos * a.qk_cs + d] =
+                          __float2bfloat16_rn(x);
+            continue;
+        }
+        float* red = qsm + parity * (4 + 128);
+        float* xs = red + 4;
+        const float s = warp_sum(x * x);
+        if (lane == 0) red[quarter] = s;
+        epi_bar();
+        const float ss = (red[0] + red[2]) + (red[1] + red[3]);  // the block_sum order
+        const float inv = rsqrtf(ss / 128.f + a.qk_eps);
+        const float xn = __bfloat162float(__float2bfloat16_rn(
+            __bfloat162float(__float2bfloat16_rn(x * inv)) * wgt));
+        xs[d] = xn;
+        epi_bar();
+        const float other = xs[(d + 64) & 127];
+        const float rotated = d < 64 ? -other : other;
+        const float y = __bfloat162float(__float2bfloat16_rn(xn * c)) +
+                        __bfloat162float(__float2bfloat16_rn(rotated * sn));
+        if (live) {
+            if (is_q)
+                a.qk_q[((int64_t)b * hq + head) * 128 + d] = __float2bfloat16_rn(y);
+            else
+                a.qk_k[(int64_t)b * a.qk_cb + (int64_t)(head - hq) * a.qk_ch + pos * a.qk_cs + d] =
+                    __float2bfloat16_rn(y);
+        }
+        parity ^= 1;
+    }
+}
 
 // The fused all-reduce's final value of output (m, n): this rank's fp32 value into the tile's
 // slot of every rank of the group (the sum follows once every rank has published the tile).
@@ -439,6 +510,8 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
           GemmArgs a) {
     constexpr bool AMAX = MODE == kModeAmax;
     constexpr bool AR = MODE == kModeAr;
+    constexpr bool QKV = MODE == kModeQkv;
+    static_assert(!QKV || NT == 16, "the fused QKV epilogue takes decode token tiles");
     using L = TcSmem<NT>;
     constexpr int STAGES = L::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -466,6 +539,8 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
     volatile uint32_t* last_flag = misc + 2;
     volatile uint32_t* ar_call = misc + 3;  // fused all-reduce: this tile's call number
     volatile uint32_t* ar_ok = misc + 4;    // fused all-reduce: every rank's tile arrived
+    float* qk_smem = reinterpret_cast<float*>(gbase + L::kMiscOff + 32);  // kModeQkv epilogue
+    int qk_parity = 0;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
@@ -676,7 +751,14 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             // tcgen05.ld is a warp-wide instruction: every lane of the warp executes it, and
             // only the stores depend on the lane's row (n < N) or on what it collected.
             if (whole) {
-                if (ok) {
+                if constexpr (QKV) {
+                    // barriers inside: every thread takes every column, whatever `ok`
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = 0.f;
+                    if (ok) tmem_ld16(taddr, v);
+                    qkv_rope_chunk(a, v, mcount, m0, sg.t, row, q, lane, ok, qk_smem, qk_parity);
+                } else if (ok) {
 #pragma unroll 1
                     for (int c0 = 0; c0 < NT; c0 += 16) {
                         if (c0 >= mcount) break;  // warp-uniform
@@ -786,6 +868,16 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                             }
                         }
                     }
+                } else if (QKV) {
+                    // the decode token tile: partners' partials were summed into psum above
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = 0.f;
+                    if (ok) tmem_ld16(taddr, v);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] += psum[j];
+                    qkv_rope_chunk(a, v, mcount, m0, sg.t, row, q, lane, ok && got, qk_smem,
+                                   qk_parity);
                 } else if (ok) {
 #pragma unroll 1
                     for (int c0 = 0; c0 < NT; c0 += 16) {
@@ -1071,8 +1163,9 @@ static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
         P.G = (int)G;
     }
     a.coresident = P.G <= resident[dev] ? 1 : 0;
-    // The fused all-reduce finishes every tile in the waiting protocol: the whole grid resident.
-    if (MODE == kModeAr && !a.coresident) return NK_ERR_PLAN;
+    // The fused all-reduce and QKV epilogues finish every tile in the waiting protocol: the
+    // whole grid resident.
+    if ((MODE == kModeAr || MODE == kModeQkv) && !a.coresident) return NK_ERR_PLAN;
     const int grid = P.G;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
@@ -1105,8 +1198,11 @@ int launch_tc(const nk_plan& p, const GemmArgs& in, cudaStream_t s) {
     CUtensorMap mw, mx;
     if (make_map(&mw, a.w, a.N, a.K, a.ldw, kTcRows) != NK_OK) return NK_ERR_ALIGN;
     if (make_map(&mx, a.x, a.M, a.K, a.ldx, nt) != NK_OK) return NK_ERR_ALIGN;
-    const int mode = a.amax_keys ? kModeAmax : (a.ar_world > 0 ? kModeAr : kModePlain);
+    const int mode = a.amax_keys ? kModeAmax
+                   : a.ar_world > 0 ? kModeAr
+                   : a.qk_q ? kModeQkv : kModePlain;
     switch (nt * 4 + mode) {
+        case 16 * 4 + kModeQkv: return launch_tc_t<16, kModeQkv>(p, a, mw, mx, s);
         case 16 * 4 + kModePlain: return launch_tc_t<16, kModePlain>(p, a, mw, mx, s);
         case 16 * 4 + kModeAmax: return launch_tc_t<16, kModeAmax>(p, a, mw, mx, s);
         case 16 * 4 + kModeAr: return launch_tc_t<16, kModeAr>(p, a, mw, mx, s);
@@ -1120,7 +1216,7 @@ int launch_tc(const nk_plan& p, const GemmArgs& in, cudaStream_t s) {
         case 128 * 4 + kModeAmax: return launch_tc_t<128, kModeAmax>(p, a, mw, mx, s);
         case 256 * 4 + kModePlain: return launch_tc_t<256, kModePlain>(p, a, mw, mx, s);
         case 256 * 4 + kModeAmax: return launch_tc_t<256, kModeAmax>(p, a, mw, mx, s);
-        default: return NK_ERR_PLAN;  // the fused all-reduce takes token tiles of up to 64
+        default: return NK_ERR_PLAN;  // fused all-reduce: token tiles <= 64; fused QKV: 16
     }
 }
 

@@ -6,6 +6,9 @@ host synchronisation. Each replaces one of the reference engine's Triton wrapper
 
 * ``rmsnorm``            <- ``norm_out``            (engine/kernels/rmsnorm.py:28-41)
 * ``qk_norm_rope_cache`` <- ``qk_rope_cache_out``   (engine/kernels/elementwise.py:63-78)
+* ``qkv_rope_cache``     <- ``torch.mm(norm, w.qkv, out=qkv)`` + ``qk_rope_cache_out``
+                            (engine/kernels/decode.py:54-55): the QKV linear and its consumer
+                            in one launch, qkv never stored
 * ``attention_decode``   <- ``attention_out``       (engine/kernels/attention.py:53-62)
 * ``silu_mul``           <- ``silu_mul_out``        (engine/kernels/elementwise.py:91-101)
 """
@@ -73,6 +76,41 @@ def qk_norm_rope_cache(qkv, q_norm, k_norm, cos, sin, position, q_out, k_cache, 
         k_cache.stride(1), k_cache.stride(2), float(eps), _stream(qkv))
     if st != _lib.NK_OK:
         _raise(st, "nk_qk_norm_rope_cache_bf16")
+
+
+def qkv_rope_cache(x, w_qkv_t, q_norm, k_norm, cos, sin, position, q_out, k_cache, v_cache,
+                   heads: int, kv_heads: int, eps: float, plan=None):
+    """``qk_norm_rope_cache`` of ``x @ w_qkv_t`` without storing the product: the QKV linear
+    (``w_qkv_t`` = Wqkv.t() of the packed row-major weight, as ``mm`` takes it) whose kernel
+    finishes each 128-row head tile with that head's RMSNorm + RoPE and writes queries, keys
+    and values where the attention reads them. Same bits as ``mm`` then
+    ``qk_norm_rope_cache``. Decode batches of up to 16 tokens."""
+    from . import gemm
+    gemm._check_tensor(x, "x")
+    gemm._check_tensor(w_qkv_t, "w_qkv_t")
+    _bf16_cuda(q_norm, k_norm, cos, sin, q_out, k_cache, v_cache)
+    _need(position.is_cuda and position.dtype == torch.int64, "position: CUDA int64 tensor")
+    M, K = x.shape
+    K2, N = w_qkv_t.shape
+    _need(K2 == K and N == (heads + 2 * kv_heads) * HEAD_DIM,
+          f"qkv_rope_cache: x [{M}, {K}] and w_qkv_t [{K2}, {N}] for {heads}+2x{kv_heads} heads")
+    _need(1 <= M <= 16, "qkv_rope_cache: decode batches of 1 to 16 tokens")
+    _need(x.stride(1) == 1 and w_qkv_t.stride(0) == 1 and q_out.is_contiguous()
+          and cos.is_contiguous() and sin.is_contiguous() and k_cache.stride(3) == 1
+          and v_cache.stride() == k_cache.stride(), "qkv_rope_cache: unsupported layout")
+    plan = plan or gemm.plan_for(M, N, K)
+    dev = x.device
+    stream = torch.cuda.current_stream(dev)
+    ws = gemm.workspace(plan.ws_bytes, dev, stream) if plan.ws_bytes else None
+    st = _lib.load().nk_gemm_bf16_qkv_rope_cache(
+        x.data_ptr(), x.stride(0) if M > 1 else K, w_qkv_t.data_ptr(), w_qkv_t.stride(1), M, N, K,
+        plan._ref, ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+        q_norm.data_ptr(), k_norm.data_ptr(), cos.data_ptr(), sin.data_ptr(), position.data_ptr(),
+        q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), heads, kv_heads,
+        k_cache.shape[2], k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), float(eps),
+        stream.cuda_stream)
+    if st != _lib.NK_OK:
+        _raise(st, "nk_gemm_bf16_qkv_rope_cache")
 
 
 def attention_workspace(batch: int, heads: int, capacity: int, device) -> torch.Tensor:

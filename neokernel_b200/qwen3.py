@@ -257,11 +257,18 @@ def layer_step_fused(st: DecodeState, w: LayerWeights, k_cache, v_cache, d: Qwen
     fuse_norm_residual scheme (engine/kernels/decode.py:42-68): the down projection's output
     stays in ``branch`` and the next RMSNorm adds it into ``x`` (``carry``)."""
     from . import decode_ops as ops
+    from . import gemm
     row_linear = row_linear or linear
     ops.rmsnorm(st.x, w.input_norm, st.norm, d.eps, branch=st.branch if carry else None)
-    linear(st.norm, w.qkv, out=st.qkv)                                   # decode.py:54
-    ops.qk_norm_rope_cache(st.qkv, w.q_norm, w.k_norm, st.cos, st.sin, st.position, st.q,
-                           k_cache, v_cache, d.heads, d.kv_heads, d.eps)
+    if linear is gemm.mm and st.batch <= 16:
+        # decode.py:54-55 in one launch: the QKV linear finishes each head with its norm, RoPE
+        # and cache write (qkv is not stored)
+        ops.qkv_rope_cache(st.norm, w.qkv, w.q_norm, w.k_norm, st.cos, st.sin, st.position,
+                           st.q, k_cache, v_cache, d.heads, d.kv_heads, d.eps)
+    else:
+        linear(st.norm, w.qkv, out=st.qkv)                               # decode.py:54
+        ops.qk_norm_rope_cache(st.qkv, w.q_norm, w.k_norm, st.cos, st.sin, st.position, st.q,
+                               k_cache, v_cache, d.heads, d.kv_heads, d.eps)
     ops.attention_decode(st.q, k_cache, v_cache, st.position, st.attn, st.attn_ws,
                          d.heads, d.kv_heads)
     row_linear(st.attn, w.o, out=st.branch)                              # decode.py:58
