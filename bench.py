@@ -1012,7 +1012,8 @@ def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, war
     this run: QKV/gate_up split by column, o_proj/down by K with their fp32 partials summed
     across ranks, lm_head by vocabulary; one CUDA graph per batch; KV length 2048. The
     product ("auto") fuses each K-slice linear with the rank-order sum over NVLink peer memory
-    (nk_gemm_bf16_allreduce) for batches up to 64; at N > 1 the step with the unfused pair
+    (nk_gemm_bf16_allreduce) for batches up to 8 (NCCL's all-reduce above); at N > 1 the step
+    with the unfused pair
     (mm_f32, nk_allreduce_bf16) and with NCCL's all-reduce are timed beside it. tok/s counts
     each sequence's token once (the ranks share one model)."""
     from neokernel_b200 import qwen3, tp
@@ -1059,7 +1060,8 @@ def tp_decode_bench(nk, dev, batches, world, rank, local, kv=2048, steps=10, war
             "batches_nccl_allreduce": out.get("nccl"),
             "collectives": "o_proj and down: each rank's K slice fused with the rank-order sum "
                            "over NVLink peer memory in one launch (nk_gemm_bf16_allreduce) for "
-                           "batches up to 64; the 'peer' arm launches mm_f32 then "
+                           "batches up to 8 (mm_f32 + NCCL all-reduce above); the 'peer' arm "
+                           "launches mm_f32 then "
                            "nk_allreduce_bf16, the 'nccl' arm mm_f32 then NCCL all-reduce; "
                            "lm_head: each shard's argmax in its launch (nk_gemm_bf16_argmax), "
                            "NCCL all-gather of (max, index); all captured in the CUDA graph"}

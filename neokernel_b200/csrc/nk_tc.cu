@@ -178,15 +178,26 @@ __device__ __forceinline__ uint64_t global_ns() {
 
 // Bounded wait until *count >= target (another CTA of this grid increments it after
 // publishing). Gives up after ~2 s, recording NK_ERR_TIMEOUT; returns whether it was reached.
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Count one more published partial of a tile: a release, so every store the CTA made before
+// the barrier that precedes this call (its partial) is visible to whoever acquires the count.
+__device__ __forceinline__ void count_release(unsigned* count) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(count) : "memory");
+}
+
 __device__ __forceinline__ bool spin_until_count(const unsigned* count, unsigned target) {
-    const volatile unsigned* c = count;
     const uint64_t t0 = global_ns();
-    while (*c < target) {
+    while (ld_acquire_gpu(count) < target) {
         if (global_ns() - t0 > 2000000000ull) {
             atomicExch(&g_error, NK_ERR_TIMEOUT);
             return false;
         }
-        __nanosleep(64);
+        __nanosleep(32);
     }
     return true;
 }
@@ -225,12 +236,15 @@ __host__ __device__ constexpr uint32_t tc_idesc(int m, int n) {
 #define NK_TC_L2_PROMO CU_TENSOR_MAP_L2_PROMOTION_L2_256B
 #endif
 
-// Shared memory of the fused QKV epilogue (kModeQkv, below): per column, the four warps' sums of
-// squares and the normalised head (for the RoPE partner element), double-buffered by column
-// parity.
+// Shared memory of the fused QKV epilogue (kModeQkv, below) for a head in the middle of a CTA's
+// range, whose ring is still in use: one column at a time, (4 warp sums + 128 elements) for two
+// columns in turn. It keeps the kernel within the footprint that lets two launches share an SM;
+// a head finished last (the usual case: heads are split over several CTAs) uses the idle ring.
 constexpr int kQkvSmemBytes = 2 * (4 + 128) * 4;
 
-template <int NT>
+// EXTRA: bytes after the barriers and flags for a mode's own use (they do not change the
+// number of stages the budget gives).
+template <int NT, int EXTRA = 0>
 struct TcSmem {
     static constexpr int kBoxA = kTcRows * kTcBox * 2;  // 16 KB: 128 weight rows x 128 B
     static constexpr int kBoxB = NT * kTcBox * 2;       // NT tokens x 128 B
@@ -245,7 +259,7 @@ struct TcSmem {
     static constexpr int kNumBars = 2 * kStages + 4 + kPartBars;  // full, empty, tfull[2], tempty[2], part
     static constexpr int kMiscOff = kBarOff + kNumBars * 8;
     // tmem slot, abort, last, all-reduce call, ok; then the fused QKV epilogue's buffers
-    static constexpr int kBytes = kMiscOff + 32 + kQkvSmemBytes;
+    static constexpr int kBytes = kMiscOff + 32 + EXTRA;
     static constexpr int kAlloc = kBytes + 1024;         // slack to align the base to 1 KB
     static constexpr int kTmemCols = 2 * NT < 32 ? 32 : 2 * NT;  // two accumulators
     // 228 KB of shared memory per SM, 1 KB of it reserved per resident CTA
@@ -283,18 +297,29 @@ __device__ __forceinline__ void clear_slot(uint64_t* p) {
 
 // ps[j] += the plain fp32 partials of ranks 1, 2, ..., nseg-1 (in that order) at token
 // columns c0 + j < mcount of one tile row (part0: the row's rank-0, column-0 value); the caller
-// has seen the tile's count complete.
+// has seen the tile's count complete. The loads of up to six ranks for eight columns are in
+// flight together, so a tile shared by seven CTAs costs two L2 round trips, not six.
 __device__ __forceinline__ void sum_partials16(const float* part0, int part_cols, int c0,
                                                int nseg, int mcount, float (&ps)[16]) {
-#pragma unroll 2
-    for (int r = 1; r < nseg; ++r) {
-        const float* pr = part0 + ((size_t)r * part_cols + c0) * kTcRows;
-        float p[16];
+    constexpr int RB = 6;
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-            p[j] = (c0 + j < mcount) ? __ldcg(pr + (size_t)j * kTcRows) : 0.f;
+    for (int h = 0; h < 16; h += 8) {
+        if (c0 + h >= mcount) break;
+        for (int r0 = 1; r0 < nseg; r0 += RB) {
+            float p[RB][8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) ps[j] += p[j];
+            for (int i = 0; i < RB; ++i) {
+                const float* pr = part0 + ((size_t)(r0 + i) * part_cols + c0 + h) * kTcRows;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    p[i][j] = (r0 + i < nseg && c0 + h + j < mcount) ? __ldcg(pr + (size_t)j * kTcRows)
+                                                                     : 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < RB; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) ps[h + j] += p[i][j];
+        }
     }
 }
 
@@ -435,42 +460,120 @@ __device__ __forceinline__ Segment segment_at(int64_t u, int64_t u_end, int KB) 
 //               and values where the attention reads them (decode token tiles only).
 constexpr int kModePlain = 0, kModeAmax = 1, kModeAr = 2, kModeQkv = 3;
 
-// The kModeQkv epilogue for `cols` token columns of one head tile (values v, tokens b0 + j):
-// exactly nk_qk_norm_rope_cache_bf16 (nk_decode.cu) applied to the bf16-rounded outputs, with
-// the same sum-of-squares order. Every epilogue thread calls it for the same columns (it holds
-// CTA-wide barriers); `live` only gates the stores.
-__device__ __forceinline__ void qkv_rope_chunk(const GemmArgs& a, const float (&v)[16], int cols,
-                                               int b0, int head, int d, int quarter, int lane,
-                                               bool live, float* qsm, int& parity) {
-    const int hq = a.qk_hq, hkv = a.qk_hkv;
-    const int64_t pos = *a.qk_pos;
-    const bool pos_ok = pos >= 0 && pos < a.qk_cap;
-    if (!pos_ok && head == 0 && d == 0 && b0 == 0) atomicExch(&g_error, NK_ERR_RANGE);
-    live = live && pos_ok;
-    const bool is_q = head < hq;
-    const bool is_v = head >= hq + hkv;  // value heads follow the keys
-    float wgt = 0.f, c = 0.f, sn = 0.f;
-    if (!is_v) {
-        wgt = __bfloat162float(is_q ? a.qk_qnorm[d] : a.qk_knorm[d]);
-        const int64_t p = pos_ok ? pos : 0;
-        c = __bfloat162float(a.qk_cos[p * 128 + d]);
-        sn = __bfloat162float(a.qk_sin[p * 128 + d]);
+// What the kModeQkv epilogue of one head needs besides the accumulator, loaded while the
+// head's last MMAs still run: the decode position and, for a query or key head, this thread's
+// gain and rotary cos/sin at that position.
+struct QkvOperands {
+    int64_t pos;
+    bool pos_ok, is_q, is_v;
+    float wgt, c, sn;
+};
+
+__device__ __forceinline__ QkvOperands qkv_operands(const GemmArgs& a, int head, int d) {
+    QkvOperands o;
+    o.pos = *a.qk_pos;
+    o.pos_ok = o.pos >= 0 && o.pos < a.qk_cap;
+    o.is_q = head < a.qk_hq;
+    o.is_v = head >= a.qk_hq + a.qk_hkv;  // value heads follow the keys
+    o.wgt = o.c = o.sn = 0.f;
+    if (!o.is_v) {
+        o.wgt = __bfloat162float(o.is_q ? a.qk_qnorm[d] : a.qk_knorm[d]);
+        const int64_t p = o.pos_ok ? o.pos : 0;
+        o.c = __bfloat162float(a.qk_cos[p * 128 + d]);
+        o.sn = __bfloat162float(a.qk_sin[p * 128 + d]);
     }
+    return o;
+}
+
+// The kModeQkv epilogue for the `cols` token columns of one head tile (values v, tokens
+// b0 + j): exactly nk_qk_norm_rope_cache_bf16 (nk_decode.cu) applied to the bf16-rounded
+// outputs, with the same sum-of-squares order, so the same bits. All columns at once: each
+// warp reduces its 32 rows of every column, one barrier, every thread normalises its element
+// of every column, one barrier, the RoPE partner comes from shared memory. `sm` holds
+// 16 x (4 + 128) floats. Every epilogue thread calls it (it holds CTA-wide barriers); `live`
+// only gates the stores.
+__device__ __forceinline__ void qkv_rope_tile(const GemmArgs& a, const QkvOperands& o,
+                                              float (&v)[16], int cols, int b0, int head, int d,
+                                              int quarter, int lane, bool live, float* sm) {
+    const int hq = a.qk_hq, hkv = a.qk_hkv;
+    if (!o.pos_ok && head == 0 && d == 0 && b0 == 0) atomicExch(&g_error, NK_ERR_RANGE);
+    live = live && o.pos_ok;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));  // bf16 qkv
+    if (o.is_v) {
+        const int kh = head - hq - hkv;
+        if (live)
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (j < cols)
+                    a.qk_v[(int64_t)(b0 + j) * a.qk_cb + (int64_t)kh * a.qk_ch + o.pos * a.qk_cs + d] =
+                        __float2bfloat16_rn(v[j]);
+        return;
+    }
+    float* red = sm;            // [16 columns][4 quarters]
+    float* xs = sm + 16 * 4;    // [16 columns][128]
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const float s = warp_sum(v[j] * v[j]);
+        if (lane == 0 && j < cols) red[j * 4 + quarter] = s;
+    }
+    epi_bar();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        if (j < cols) {
+            const float* r = red + j * 4;
+            const float ss = (r[0] + r[2]) + (r[1] + r[3]);  // the block_sum order
+            const float inv = rsqrtf(ss / 128.f + a.qk_eps);
+            v[j] = __bfloat162float(__float2bfloat16_rn(
+                __bfloat162float(__float2bfloat16_rn(v[j] * inv)) * o.wgt));  // normalised
+            xs[j * 128 + d] = v[j];
+        }
+    }
+    epi_bar();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        if (j < cols) {
+            const float other = xs[j * 128 + ((d + 64) & 127)];
+            const float rotated = d < 64 ? -other : other;
+            const float y = __bfloat162float(__float2bfloat16_rn(v[j] * o.c)) +
+                            __bfloat162float(__float2bfloat16_rn(rotated * o.sn));
+            if (live) {
+                const int b = b0 + j;
+                if (o.is_q)
+                    a.qk_q[((int64_t)b * hq + head) * 128 + d] = __float2bfloat16_rn(y);
+                else
+                    a.qk_k[(int64_t)b * a.qk_cb + (int64_t)(head - hq) * a.qk_ch + o.pos * a.qk_cs +
+                           d] = __float2bfloat16_rn(y);
+            }
+        }
+    }
+    epi_bar();  // `sm` is free again for the next head
+}
+
+// qkv_rope_tile for a head whose CTA's ring is still in use: the same arithmetic, one column
+// at a time through `sm` (2 x (4 + 128) floats, alternating between columns).
+__device__ __forceinline__ void qkv_rope_columns(const GemmArgs& a, const QkvOperands& o,
+                                                 float (&v)[16], int cols, int b0, int head,
+                                                 int d, int quarter, int lane, bool live,
+                                                 float* sm) {
+    const int hq = a.qk_hq, hkv = a.qk_hkv;
+    if (!o.pos_ok && head == 0 && d == 0 && b0 == 0) atomicExch(&g_error, NK_ERR_RANGE);
+    live = live && o.pos_ok;
 #pragma unroll 1
     for (int j = 0; j < cols; ++j) {
         float x = 0.f;
 #pragma unroll
         for (int i = 0; i < 16; ++i)
             if (i == j) x = v[i];
-        x = __bfloat162float(__float2bfloat16_rn(x));  // the linear's bf16 output
+        x = __bfloat162float(__float2bfloat16_rn(x));  // bf16 qkv
         const int b = b0 + j;
-        if (is_v) {
-            const int kh = head - hq - hkv;
-            if (live) a.qk_v[(int64_t)b * a.qk_cb + (int64_t)kh * a.qk_ch + pos * a.qk_cs + d] =
-                          __float2bfloat16_rn(x);
+        if (o.is_v) {
+            if (live)
+                a.qk_v[(int64_t)b * a.qk_cb + (int64_t)(head - hq - hkv) * a.qk_ch +
+                       o.pos * a.qk_cs + d] = __float2bfloat16_rn(x);
             continue;
         }
-        float* red = qsm + parity * (4 + 128);
+        float* red = sm + (j & 1) * (4 + 128);
         float* xs = red + 4;
         const float s = warp_sum(x * x);
         if (lane == 0) red[quarter] = s;
@@ -478,22 +581,22 @@ __device__ __forceinline__ void qkv_rope_chunk(const GemmArgs& a, const float (&
         const float ss = (red[0] + red[2]) + (red[1] + red[3]);  // the block_sum order
         const float inv = rsqrtf(ss / 128.f + a.qk_eps);
         const float xn = __bfloat162float(__float2bfloat16_rn(
-            __bfloat162float(__float2bfloat16_rn(x * inv)) * wgt));
+            __bfloat162float(__float2bfloat16_rn(x * inv)) * o.wgt));
         xs[d] = xn;
         epi_bar();
         const float other = xs[(d + 64) & 127];
         const float rotated = d < 64 ? -other : other;
-        const float y = __bfloat162float(__float2bfloat16_rn(xn * c)) +
-                        __bfloat162float(__float2bfloat16_rn(rotated * sn));
+        const float y = __bfloat162float(__float2bfloat16_rn(xn * o.c)) +
+                        __bfloat162float(__float2bfloat16_rn(rotated * o.sn));
         if (live) {
-            if (is_q)
+            if (o.is_q)
                 a.qk_q[((int64_t)b * hq + head) * 128 + d] = __float2bfloat16_rn(y);
             else
-                a.qk_k[(int64_t)b * a.qk_cb + (int64_t)(head - hq) * a.qk_ch + pos * a.qk_cs + d] =
+                a.qk_k[(int64_t)b * a.qk_cb + (int64_t)(head - hq) * a.qk_ch + o.pos * a.qk_cs + d] =
                     __float2bfloat16_rn(y);
         }
-        parity ^= 1;
     }
+    if (!o.is_v) epi_bar();  // `sm` is free again for the next head
 }
 
 // The fused all-reduce's final value of output (m, n): this rank's fp32 value into the tile's
@@ -512,7 +615,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
     constexpr bool AR = MODE == kModeAr;
     constexpr bool QKV = MODE == kModeQkv;
     static_assert(!QKV || NT == 16, "the fused QKV epilogue takes decode token tiles");
-    using L = TcSmem<NT>;
+    using L = TcSmem<NT, QKV ? kQkvSmemBytes : 0>;
     constexpr int STAGES = L::kStages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -540,7 +643,6 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
     volatile uint32_t* ar_call = misc + 3;  // fused all-reduce: this tile's call number
     volatile uint32_t* ar_ok = misc + 4;    // fused all-reduce: every rank's tile arrived
     float* qk_smem = reinterpret_cast<float*>(gbase + L::kMiscOff + 32);  // kModeQkv epilogue
-    int qk_parity = 0;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
@@ -707,6 +809,12 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             // Failure-detection tests only: this CTA keeps its partial to itself, so the tile's
             // finisher's bounded wait runs out (NK_ERR_TIMEOUT) instead of completing.
             const bool withhold = wait_mode && rank == 1 && sg.t == a.withhold_tile;
+            // Fused QKV epilogue: the head's position, gain and rotary operands, loaded while the
+            // head's last MMAs still run.
+            QkvOperands qo{};
+            if constexpr (QKV) {
+                if (whole || finisher) qo = qkv_operands(a, sg.t, row);
+            }
             // Fused all-reduce: the call number of this output tile (its progress counter in
             // this rank's receive buffer, plus one) picks the set of flags and slots.
             unsigned ar_e = 0;
@@ -729,10 +837,11 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             for (int j = 0; j < 16; ++j) psum[j] = 0.f;
             bool got = true;
             if (finisher && !tagged) {
+                // one thread acquires the count; the barrier orders every thread's partial
+                // loads (through L2) after that acquire
                 if (ep == 0)
                     *last_flag = spin_until_count(a.tickets + sg.t, (unsigned)(nseg - 1)) ? 1u : 0u;
                 epi_bar();
-                __threadfence();
                 got = *last_flag != 0u;
             }
             if constexpr (NT == 16) {
@@ -757,7 +866,13 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = 0.f;
                     if (ok) tmem_ld16(taddr, v);
-                    qkv_rope_chunk(a, v, mcount, m0, sg.t, row, q, lane, ok, qk_smem, qk_parity);
+                    // a head finished last has the idle ring to work in; one in the middle of
+                    // this CTA's range (whose ring still streams) goes column by column
+                    if (u >= u_end)
+                        qkv_rope_tile(a, qo, v, mcount, m0, sg.t, row, q, lane, ok,
+                                      reinterpret_cast<float*>(gbase));
+                    else
+                        qkv_rope_columns(a, qo, v, mcount, m0, sg.t, row, q, lane, ok, qk_smem);
                 } else if (ok) {
 #pragma unroll 1
                     for (int c0 = 0; c0 < NT; c0 += 16) {
@@ -876,8 +991,9 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                     if (ok) tmem_ld16(taddr, v);
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] += psum[j];
-                    qkv_rope_chunk(a, v, mcount, m0, sg.t, row, q, lane, ok && got, qk_smem,
-                                   qk_parity);
+                    // the finishing segment is this CTA's last: its ring is idle
+                    qkv_rope_tile(a, qo, v, mcount, m0, sg.t, row, q, lane, ok && got,
+                                  reinterpret_cast<float*>(gbase));
                 } else if (ok) {
 #pragma unroll 1
                     for (int c0 = 0; c0 < NT; c0 += 16) {
@@ -914,9 +1030,9 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_tempty + 8 * buf);
             if (!whole && wait_mode && !tagged && rank > 0) {
-                __threadfence();  // this CTA's partial stores, before the count that publishes them
+                // this CTA's partial stores (ordered before the barrier), then one release
                 epi_bar();
-                if (ep == 0 && !withhold) atomicAdd(a.tickets + sg.t, 1u);
+                if (ep == 0 && !withhold) count_release(a.tickets + sg.t);
             } else if (!whole && !wait_mode) {
                 // Without a co-resident grid every rank publishes plain partials (rank 0 above as
                 // well) and the CTA whose arrival completes the tile's count sums them, in the
@@ -1100,7 +1216,7 @@ int tc_ctas_per_sm(int nt) {
 // CTA blocks in tcgen05.alloc), and capped at the per-SM count the stage budget assumes.
 template <int NT, int MODE>
 static int tc_resident_per_sm(int dev) {
-    using L = TcSmem<NT>;
+    using L = TcSmem<NT, MODE == kModeQkv ? kQkvSmemBytes : 0>;
     cudaFuncAttributes fa;
     int smem_sm = 0, reserved = 0, regs_sm = 0, thr_sm = 0;
     if (cudaFuncGetAttributes(&fa, tc_kernel<NT, MODE>) != cudaSuccess ||
@@ -1129,7 +1245,7 @@ static int tc_resident_per_sm(int dev) {
 template <int NT, int MODE>
 static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
                        const CUtensorMap& mx, cudaStream_t s) {
-    using L = TcSmem<NT>;
+    using L = TcSmem<NT, MODE == kModeQkv ? kQkvSmemBytes : 0>;
     static int resident[64] = {};  // co-resident CTAs per device (0 = not yet counted)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return NK_ERR_CUDA;

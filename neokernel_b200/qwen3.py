@@ -80,6 +80,14 @@ QWEN3_32B = Qwen3Dims(5120, 25600, 64, 8, 128, 64, 151936)
 
 INITS = ("decisive", "reference")
 
+# True: the fused decode step runs the QKV linear and its q/k-norm + RoPE + cache consumer as
+# one launch (nk_gemm_bf16_qkv_rope_cache) when the linear is neokernel_b200.mm. Off by
+# default: measured on B200 (Qwen3-8B, KV 1024, CUDA graph), the step takes 3.61 / 4.59 ms at
+# batch 1 / 16 with it and 3.37 / 4.25 ms with the two launches — the consumer then runs in
+# the tail of the linear's finishing CTAs (one per head, after the split-K sum) instead of as
+# a separate, fully parallel launch that overlaps the linear's tail.
+FUSE_QKV = False
+
 
 def _randn(shape, gen, device, std=0.02):
     t = torch.randn(shape, generator=gen, device=device, dtype=torch.float32)
@@ -260,7 +268,7 @@ def layer_step_fused(st: DecodeState, w: LayerWeights, k_cache, v_cache, d: Qwen
     from . import gemm
     row_linear = row_linear or linear
     ops.rmsnorm(st.x, w.input_norm, st.norm, d.eps, branch=st.branch if carry else None)
-    if linear is gemm.mm and st.batch <= 16:
+    if FUSE_QKV and linear is gemm.mm and st.batch <= 16:
         # decode.py:54-55 in one launch: the QKV linear finishes each head with its norm, RoPE
         # and cache write (qkv is not stored)
         ops.qkv_rope_cache(st.norm, w.qkv, w.q_norm, w.k_norm, st.cos, st.sin, st.position,
