@@ -226,6 +226,12 @@ __host__ __device__ constexpr uint32_t tc_idesc(int m, int n) {
 #ifndef NK_TC_SMEM_SMALL
 #define NK_TC_SMEM_SMALL (110 * 1024)  // token tiles <= 64: two CTAs per SM
 #endif
+#ifndef NK_TC_SMALL_MAX_NT
+// Widest token tile given the two-per-SM budget. Token tiles of 64 (the M = 33..64 verify
+// batches) take the large ring: measured on B200, verify M = 64 QKV 20.6 -> 18.8 us, o_proj
+// 18.1 -> 16.8, down 30.6 -> 27.2, gate_up 41.5 -> 42.0.
+#define NK_TC_SMALL_MAX_NT 32
+#endif
 #ifndef NK_TC_SMEM_LARGE
 #define NK_TC_SMEM_LARGE (200 * 1024)  // token tiles >= 128: one CTA per SM
 #endif
@@ -251,7 +257,7 @@ struct TcSmem {
     static constexpr int kA = kTcUK * kBoxA;
     static constexpr int kB = kTcUK * kBoxB;
     static constexpr int kStage = kA + kB;
-    static constexpr int kBudget = NT <= 64 ? NK_TC_SMEM_SMALL : NK_TC_SMEM_LARGE;
+    static constexpr int kBudget = NT <= NK_TC_SMALL_MAX_NT ? NK_TC_SMEM_SMALL : NK_TC_SMEM_LARGE;
     static constexpr int kStagesFit = (kBudget - 2048) / kStage;
     static constexpr int kStages = kStagesFit > 8 ? 8 : (kStagesFit < 2 ? 2 : kStagesFit);
     static constexpr int kBarOff = kStages * kStage;
@@ -268,13 +274,14 @@ struct TcSmem {
     static_assert(kBoxB % 1024 == 0, "activation boxes must keep 1 KB swizzle-atom alignment");
 };
 
-// Partials of shared tiles. For decode-sized launches (M <= NK_TC_TAG_MAX_M) they live in
-// 64-bit slots {fp32 value, tag}: a rank publishes a value and its tag in one store, so a
-// reader that sees the tag has the value without a fence, a count or a second round trip, and
-// the reader clears the slot after use. The tag is a signalling-NaN bit pattern, which no
-// arithmetic produces, so no value left by another plan, launch or kernel family can pose as
-// a published slot. Larger launches, whose partials would need many slot rounds, publish
-// plain fp32 followed by a fence and the tile's count.
+// Partials of shared tiles. For decode-sized launches (M <= NK_TC_TAG_MAX_M, with few enough
+// slots to poll, see the epilogue) they live in 64-bit slots {fp32 value, tag}: a rank
+// publishes a value and its tag in one store, so a reader that sees the tag has the value
+// without a fence, a count or a second round trip, and the reader clears the slot after use.
+// The tag is a signalling-NaN bit pattern, which no arithmetic produces, so no value left by
+// another plan, launch or kernel family can pose as a published slot. Other launches, whose
+// partials would need many slot rounds, publish plain fp32 and then the tile's count (one
+// release per CTA).
 #ifndef NK_TC_TAG_MAX_M
 #define NK_TC_TAG_MAX_M 8
 #endif
@@ -786,7 +793,13 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
         const int row = 32 * q + lane;            // tile row owned by this thread
         const uint32_t tlane = (uint32_t)(32 * q) << 16;
         const bool wait_mode = a.coresident != 0;
-        const bool tagged = wait_mode && a.M <= NK_TC_TAG_MAX_M;  // the same for every CTA
+        // Tagged slots cost rank 0 a poll of every partner's slot of every column; the count
+        // protocol a fixed handful of round trips. Measured on B200 (Qwen3-8B, M = 8): tagged
+        // wins QKV (11.8 vs 12.3 us) and gate_up (33.4 vs 33.7), loses o_proj (10.7 vs 9.7)
+        // and down (20.8 vs 20.3), whose tiles are shared by 7 and 6 CTAs; M <= 4 always
+        // tagged, M = 16 always counted. The same for every CTA of the launch.
+        const bool tagged = wait_mode && a.M <= NK_TC_TAG_MAX_M &&
+                            a.M * (a.segments - 1) <= 4 * NK_TC_TAG_MAX_M;
         const bool store_y = !AMAX || a.y != nullptr;            // the greedy head may skip y
         int seg = 0;
         for (int64_t u = u_begin; u < u_end; ++seg) {
