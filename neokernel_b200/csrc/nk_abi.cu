@@ -104,8 +104,8 @@ extern "C" int nk_plan_make(nk_plan* p, int M_max, int N, int K, int split_k, in
         p->tile_m = tc_token_tile(M_max);
         p->tile_n = kTcRowsPerCta;
         p->stages = tc_stages(p->tile_m);
-        p->k_step = kTcKStep;
-        const int KB = ceil_div(K, kTcKStep);
+        p->k_step = tc_kstep(p->tile_m);
+        const int KB = ceil_div(K, p->k_step);
         const int64_t T = (int64_t)ceil_div(N, p->tile_n) * ceil_div(M_max, p->tile_m);
         const int64_t U = T * KB;
         if (split_k > 0) {
@@ -114,7 +114,7 @@ extern "C" int nk_plan_make(nk_plan* p, int M_max, int N, int K, int split_k, in
             p->split_k = split;
             p->grid = (int32_t)(T * split);
             p->segments = split;
-            p->k_slice = ceil_div(KB, split) * kTcKStep;
+            p->k_slice = ceil_div(KB, split) * p->k_step;
         } else {
             // A second CTA per SM pays only while each CTA keeps enough units: below that the
             // extra split tiles cost more finishing work, and a full SM leaves no room for
@@ -128,7 +128,7 @@ extern "C" int nk_plan_make(nk_plan* p, int M_max, int N, int K, int split_k, in
             p->split_k = 0;
             p->grid = (int32_t)G;
             p->segments = (int32_t)(seg < G ? seg : G);
-            p->k_slice = (int32_t)(q * kTcKStep);
+            p->k_slice = (int32_t)(q * p->k_step);
         }
     } else {  // NK_KIND_GEMV
         p->tile_m = gemv_token_tile(M_max);

@@ -330,8 +330,10 @@ constexpr int kTcBox = 64;               // K elements per TMA box (one 128-byte
 #ifndef NK_TC_UK
 #define NK_TC_UK 2
 #endif
-constexpr int kTcBoxesPerStage = NK_TC_UK;           // TMA boxes along K per pipeline stage
-constexpr int kTcKStep = kTcBox * kTcBoxesPerStage;  // K elements per stage (one unit)
+// TMA boxes along K per pipeline stage (one "unit" of the schedule): the 256-token tile takes
+// one, so that a stage (16 KB of weights, 32 KB of tokens) still leaves four stages in flight.
+__host__ __device__ constexpr int tc_uk(int nt) { return nt >= 256 ? 1 : NK_TC_UK; }
+__host__ __device__ constexpr int tc_kstep(int nt) { return kTcBox * tc_uk(nt); }  // K per unit
 // fewest units per CTA for which the plan puts two CTAs on an SM (when both fit)
 #ifndef NK_TC_DUAL_MIN_UNITS
 #define NK_TC_DUAL_MIN_UNITS 16

@@ -39,7 +39,6 @@
 namespace nk {
 
 constexpr int kTcRows = kTcRowsPerCta;
-constexpr int kTcUK = kTcBoxesPerStage;
 constexpr int kTcThreads = 192;            // 6 warps
 constexpr int kTcEpiThreads = 128;         // warps 2..5
 constexpr uint32_t kWaitLimit = 1u << 26;  // polls before a wait gives up (seconds)
@@ -103,14 +102,6 @@ __device__ __forceinline__ void tma_load_w(uint32_t dst, const CUtensorMap* map,
         " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar), "l"(policy)
         : "memory");
-}
-
-// Prefetch one [rows x 64] tile of a tensor map into L2 (no shared memory, no completion).
-__device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int c0, int c1) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(c0), "r"(c1)
-                 : "memory");
 }
 
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
@@ -235,9 +226,6 @@ __host__ __device__ constexpr uint32_t tc_idesc(int m, int n) {
 #ifndef NK_TC_SMEM_LARGE
 #define NK_TC_SMEM_LARGE (200 * 1024)  // token tiles >= 128: one CTA per SM
 #endif
-#ifndef NK_TC_L2_AHEAD
-#define NK_TC_L2_AHEAD 0  // units of weight prefetched into L2 ahead of the ring (0 = none)
-#endif
 #ifndef NK_TC_L2_PROMO
 #define NK_TC_L2_PROMO CU_TENSOR_MAP_L2_PROMOTION_L2_256B
 #endif
@@ -254,8 +242,9 @@ template <int NT, int EXTRA = 0>
 struct TcSmem {
     static constexpr int kBoxA = kTcRows * kTcBox * 2;  // 16 KB: 128 weight rows x 128 B
     static constexpr int kBoxB = NT * kTcBox * 2;       // NT tokens x 128 B
-    static constexpr int kA = kTcUK * kBoxA;
-    static constexpr int kB = kTcUK * kBoxB;
+    static constexpr int kUK = tc_uk(NT);  // boxes along K per stage
+    static constexpr int kA = kUK * kBoxA;
+    static constexpr int kB = kUK * kBoxB;
     static constexpr int kStage = kA + kB;
     static constexpr int kBudget = NT <= NK_TC_SMALL_MAX_NT ? NK_TC_SMEM_SMALL : NK_TC_SMEM_LARGE;
     static constexpr int kStagesFit = (kBudget - 2048) / kStage;
@@ -622,6 +611,8 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
     constexpr bool AR = MODE == kModeAr;
     constexpr bool QKV = MODE == kModeQkv;
     static_assert(!QKV || NT == 16, "the fused QKV epilogue takes decode token tiles");
+    constexpr int kTcUK = tc_uk(NT);       // boxes along K per stage
+    constexpr int kTcKStep = tc_kstep(NT);  // K elements per unit
     using L = TcSmem<NT, QKV ? kQkvSmemBytes : 0>;
     constexpr int STAGES = L::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -706,20 +697,6 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                     tma_load_2d(base + i * L::kStage + L::kA + ub * L::kBoxB, &tmap_x,
                                 bar_full + 8 * i, kb * kTcKStep + ub * kTcBox, (t / a.n_tiles) * NT);
             }
-            // Rolling L2 prefetch of the weight tiles NK_TC_L2_AHEAD units ahead of the ring:
-            // DRAM keeps that many more units in flight than the ring's stages hold, and the
-            // ring's own loads then find their tiles in L2.
-            auto prefetch_unit = [&](int i) {
-                if (NK_TC_L2_AHEAD > 0 && i < n_units) {
-                    const int64_t u = u_begin + i;
-                    const int t = (int)(u / KB);
-                    const int kb = (int)(u - (int64_t)t * KB);
-#pragma unroll
-                    for (int ub = 0; ub < kTcUK; ++ub)
-                        tma_prefetch_l2(&tmap_w, kb * kTcKStep + ub * kTcBox, (t % a.n_tiles) * kTcRows);
-                }
-            };
-            for (int i = n_pre; i < n_pre + NK_TC_L2_AHEAD; ++i) prefetch_unit(i);
             int issued = n_pre;
             for (int i = n_pre; i < n_units; ++i) {
                 const int st = i % STAGES;
@@ -740,7 +717,6 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                     tma_load_2d(sa + L::kA + ub * L::kBoxB, &tmap_x, bar_full + 8 * st,
                                 kb * kTcKStep + ub * kTcBox, (t / a.n_tiles) * NT);
                 ++issued;
-                prefetch_unit(i + NK_TC_L2_AHEAD);
             }
             // Drain: every stage's last load has landed and (unless the MMA issuer gave up)
             // every MMA that read it has completed before this CTA may exit.
@@ -1314,7 +1290,7 @@ int launch_tc(const nk_plan& p, const GemmArgs& in, cudaStream_t s) {
     if (get_encoder() != NK_OK) return NK_ERR_CUDA;
     GemmArgs a = in;
     const int nt = p.tile_m;
-    const int KB = (a.K + kTcKStep - 1) / kTcKStep;
+    const int KB = (a.K + tc_kstep(nt) - 1) / tc_kstep(nt);
     const int m_tiles = (a.M + nt - 1) / nt;  // token tiles of this call (<= the plan's)
     a.n_tiles = p.n_tiles;
     a.segments = p.segments;
