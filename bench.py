@@ -693,18 +693,27 @@ def shapes_table(args):
 
 
 def split_sweep(args):
-    """--split-sweep: the Qwen3-8B decode linears at M in {1, 16} with split-K forced to every
-    value 1..16 beside the plan's balanced schedule (split 0), us per launch as in shape_rows."""
+    """--split-sweep: the Qwen3-8B decode linears (M 1..16; gate_up and lm_head at M 1 and 16)
+    and the Qwen3-0.6B layer linears (M 1, 4, 8, 16) with split-K forced to every value 1..16
+    beside the plan's own schedule (split 0: tile-aligned where the plan has slices, else
+    balanced), us per launch as in shape_rows."""
+    import neokernel_b200 as nk
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    cases = [("qwen3-8b", name, N, K, M) for name, N, K in LAYER_LINEARS + [("lm_head", VOCAB, HIDDEN)]
-             for M in (1, 16)]
-    table = {}
+    cases = [("qwen3-8b", name, N, K, M) for name, N, K in LAYER_LINEARS
+             if name in ("qkv", "o_proj", "down") for M in (1, 2, 4, 8, 16)]
+    cases += [("qwen3-8b", name, N, K, M) for name, N, K in LAYER_LINEARS + [("lm_head", VOCAB, HIDDEN)]
+              if name in ("gate_up", "lm_head") for M in (1, 16)]
+    cases += [("qwen3-0.6b", name, N, K, M) for name, N, K in QWEN3_0_6B_LINEARS for M in (1, 4, 8, 16)]
+    table, slices = {}, {}
+    for _, name, N, K, M in cases:
+        slices[f"{name} {N}x{K} M={M}"] = nk.plan_for(M, N, K).as_dict()["slices"]
     for split in range(0, 17):
         for r in shape_rows(dev, cases, reps=3, cublas=False, split=split)["rows"]:
-            table.setdefault(f"{r['linear']} M={r['M']}", {})[str(split)] = r["us"]
-    print(json.dumps({"split_sweep_us": table, "note": "split 0 = the plan's balanced "
-                      "persistent schedule; 1..16 = one CTA per (tile, K slice)"}))
+            table.setdefault(f"{r['model']} {r['linear']} M={r['M']}", {})[str(split)] = r["us"]
+    print(json.dumps({"split_sweep_us": table, "plan_slices": slices,
+                      "note": "split 0 = the plan's own schedule (tile-aligned with the plan's "
+                      "slices, else balanced persistent); 1..16 = one CTA per (tile, K slice)"}))
     return 0
 
 

@@ -84,10 +84,14 @@ typedef struct nk_plan {
     int32_t stages;      /* shared-memory pipeline depth (tensor-core kernel)          */
     int32_t n_tiles;     /* ceil(N / tile_n)                                           */
     int32_t m_tiles;     /* ceil(M_max / tile_m)                                       */
-    int32_t grid;        /* CTAs launched (tensor-core family: persistent grid)        */
+    int32_t grid;        /* CTAs launched (tensor-core family: persistent grid of the
+                            balanced schedule)                                         */
     int32_t segments;    /* most CTAs sharing one output tile (1 = no partial sums)    */
     int32_t k_step;      /* K elements per pipeline step (tensor-core family's unit)   */
-    int32_t reserved[1];
+    int32_t slices;      /* tensor-core family, 16-token tile, split_k 0: K slices per
+                            tile of the tile-aligned schedule (tiles x slices CTAs, two
+                            per SM, one wave) that launches use when all of it is
+                            resident; 0 = the balanced schedule only                   */
 } nk_plan;
 
 #define NK_PLAN_MAGIC 0x4E4B4731 /* "NKG1" */

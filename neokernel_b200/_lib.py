@@ -73,11 +73,11 @@ class NkPlan(ctypes.Structure):
         ("grid", ctypes.c_int32),
         ("segments", ctypes.c_int32),
         ("k_step", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 1),
+        ("slices", ctypes.c_int32),
     ]
 
     def as_dict(self) -> dict:
-        return {name: getattr(self, name) for name, _ in self._fields_ if name != "reserved"}
+        return {name: getattr(self, name) for name, _ in self._fields_}
 
 
 class NkError(RuntimeError):

@@ -286,6 +286,7 @@ struct GemmArgs {
     // tensor-core family only
     int n_tiles;            // ceil(N / 128)
     int segments;           // partial slots per tile
+    int seg_max;            // most CTAs sharing one tile in this launch's partition (<= segments)
     int part_cols;          // token columns per partial slot (min(NT, M_max))
     int coresident;         // 1: every CTA of the grid is resident at once (see nk_tc.cu)
     int withhold_tile;      // failure-detection tests only (nk_test_withhold_partial): the
@@ -337,6 +338,13 @@ __host__ __device__ constexpr int tc_kstep(int nt) { return kTcBox * tc_uk(nt); 
 // fewest units per CTA for which the plan puts two CTAs on an SM (when both fit)
 #ifndef NK_TC_DUAL_MIN_UNITS
 #define NK_TC_DUAL_MIN_UNITS 16
+#endif
+// the tile-aligned schedule (nk_plan.slices): on, and the fewest slices per tile it takes
+#ifndef NK_TC_ALIGNED
+#define NK_TC_ALIGNED 1
+#endif
+#ifndef NK_TC_MIN_SLICES
+#define NK_TC_MIN_SLICES 4
 #endif
 constexpr int kGenericRows = 8;          // rows per CTA in the generic kernel
 constexpr int kGenericTokens = 8;        // tokens per CTA in the generic kernel

@@ -775,7 +775,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
         // and down (20.8 vs 20.3), whose tiles are shared by 7 and 6 CTAs; M <= 4 always
         // tagged, M = 16 always counted. The same for every CTA of the launch.
         const bool tagged = wait_mode && a.M <= NK_TC_TAG_MAX_M &&
-                            a.M * (a.segments - 1) <= 4 * NK_TC_TAG_MAX_M;
+                            a.M * (a.seg_max - 1) <= 4 * NK_TC_TAG_MAX_M;
         const bool store_y = !AMAX || a.y != nullptr;            // the greedy head may skip y
         int seg = 0;
         for (int64_t u = u_begin; u < u_end; ++seg) {
@@ -930,8 +930,12 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                                       tile_part + ((size_t)(1 + i) * a.part_cols + 16 * k) * kTcRows,
                                       bytes, bar_part + 8 * h);
                     };
-                    if (ep == 0)
+                    if (ep == 0) {
+                        // the partners' stores (acquired above through the generic proxy)
+                        // before the async-proxy copies that read them
+                        asm volatile("fence.proxy.async.global;" ::: "memory");
                         for (int k = 0; k < slots; ++k) issue(k);
+                    }
 #pragma unroll 1
                     for (int k = 0; k < nchunks; ++k) {
                         const int h = k % slots;
@@ -1253,8 +1257,17 @@ static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
         resident[dev] = per_sm * sms;
     }
     TcPartition& P = a.part_map;
+    const int64_t tiles = P.U / P.KB;
     if (p.split_k > 0) {
-        P.G = (int)(P.U / P.KB) * p.split_k;
+        P.G = (int)tiles * p.split_k;
+        a.seg_max = p.split_k;
+    } else if (p.slices > 0 && tiles * p.slices <= resident[dev]) {
+        // the tile-aligned schedule: one K slice per CTA, the whole grid resident (every mode
+        // takes it, so that the fused forms add the same partials in the same order as the
+        // plain launches they replace)
+        P.split = p.slices;
+        P.G = (int)(tiles * p.slices);
+        a.seg_max = p.slices;
     } else {
         // Keep at least the plan's units per CTA, so no tile is shared by more CTAs than the
         // plan's `segments` (the workspace was sized for that); never more CTAs than can be
@@ -1266,6 +1279,9 @@ static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
         if (G > resident[dev]) G = resident[dev];
         if (G < 1) G = 1;
         P.G = (int)G;
+        const int64_t qc = P.U / G;  // fewest units a CTA holds
+        const int64_t seg = 1 + (P.KB - 1 + qc - 1) / qc;
+        a.seg_max = (int)(seg < a.segments ? seg : a.segments);
     }
     a.coresident = P.G <= resident[dev] ? 1 : 0;
     // The fused all-reduce and QKV epilogues finish every tile in the waiting protocol: the

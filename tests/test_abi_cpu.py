@@ -115,13 +115,16 @@ class Partition:
         return t * self.split + ((kb + 1) * self.split + self.KB - 1) // self.KB - 1
 
 
-def launch_partition(p, M):
-    """The partition launch_tc (nk_tc.cu) builds for a call with M tokens."""
+def launch_partition(p, M, aligned=False):
+    """The partition launch_tc (nk_tc.cu) builds for a call with M tokens: the tile-aligned
+    one (a plan with slices, whole grid resident) or the balanced one."""
     KB = -(-p.K // p.k_step)
     m_tiles = -(-M // p.tile_m)
     U = p.n_tiles * m_tiles * KB
     if p.split_k:
         return Partition(U, KB, p.n_tiles * m_tiles * p.split_k, p.split_k)
+    if aligned:
+        return Partition(U, KB, p.n_tiles * m_tiles * p.slices, p.slices)
     q = (p.n_tiles * p.m_tiles * KB) // p.grid
     G = max(1, min(p.grid, U // q))
     return Partition(U, KB, G, 0)
@@ -132,8 +135,12 @@ def check_tc_partition(p, M_max):
     assert p.k_step % 64 == 0
     if not p.split_k:
         assert p.grid <= 148 * 2
-    for M in sorted({1, M_max, max(1, M_max // 2)}):
-        P = launch_partition(p, M)
+        assert p.slices == 0 or p.n_tiles * p.m_tiles * p.slices <= 148 * 2
+    schedules = [(M, False) for M in sorted({1, M_max, max(1, M_max // 2)})]
+    if p.slices:
+        schedules += [(M, True) for M in sorted({1, M_max})]
+    for M, aligned in schedules:
+        P = launch_partition(p, M, aligned)
         assert P.begin(0) == 0 and P.begin(P.G) == P.U
         cover = []
         for c in range(P.G):
@@ -184,6 +191,23 @@ def test_tc_partition_covers_units_once(M, N, K, split):
         assert ws >= 262144 + p.n_tiles * p.m_tiles * p.segments * cols * 128 * 4
     else:
         assert ws == 0
+
+
+@pytest.mark.parametrize("M,N,K,slices", [
+    (1, 4096, 4096, 9), (8, 4096, 4096, 9), (16, 4096, 4096, 7),   # Qwen3-8B o_proj
+    (1, 6144, 4096, 6), (16, 6144, 4096, 6),                         # QKV
+    (1, 4096, 12288, 9), (16, 4096, 12288, 7),                       # down
+    (1, 24576, 4096, 0), (16, 151936, 4096, 0),                      # gate_up, lm_head
+    (64, 4096, 4096, 0), (256, 4096, 4096, 0),                       # verify tiles: one CTA per SM
+    (1, 1024, 2048, 8), (16, 1024, 3072, 7), (4, 4096, 1024, 4),     # Qwen3-0.6B
+    (1, 8, 256, 0), (32, 6144, 4096, 0)])                            # two K steps; 32-token tile
+def test_tile_aligned_slices(M, N, K, slices):
+    """The planner's tile-aligned schedule: slices = min(296 // tiles, 9 (7 above M = 8),
+    K steps // 2) when that is at least 4, for the 16-token tile (two CTAs per SM)."""
+    st, p = make(M, N, K, 0, _lib.KIND_TC)
+    assert st == 0 and p.split_k == 0
+    assert p.slices == slices, p.as_dict()
+    assert p.segments >= slices
 
 
 def test_generic_plan_for_unaligned_K():

@@ -6,7 +6,9 @@ partials; the finisher waits for them with a bounded wait (about 2 s). ``nk_test
 makes the rank-1 CTA of one tile keep its partial for the next launch, so that wait expires:
 the launch still returns, the tile's outputs are left unwritten, ``nk_device_error`` reports
 NK_ERR_TIMEOUT, and after ``nk_ws_init`` the same workspace gives the exact result again.
-Both finishing protocols are covered: tagged slots (M <= 8) and the fenced count (M > 8).
+Every finishing protocol is covered: tagged slots (M <= 8), the fenced count (M > 8) and the
+column-distributed finishing of wide token tiles (M > 32), where every finishing CTA of the tile
+waits out.
 """
 
 import ctypes
@@ -25,26 +27,35 @@ DEV = "cuda"
 
 
 def partition(p, M):
-    """(U, KB, G) of the balanced partition launch_tc builds for M tokens (nk_tc.cu)."""
+    """(U, KB, G, split) of the partition launch_tc builds for a plain call with M tokens
+    (nk_tc.cu): the tile-aligned one when the plan has slices, else the balanced one."""
     KB = -(-p.K // p.k_step)
-    U = p.n_tiles * (-(-M // p.tile_m)) * KB
+    tiles = p.n_tiles * (-(-M // p.tile_m))
+    U = tiles * KB
+    if p.slices:
+        return U, KB, tiles * p.slices, p.slices
     q = (p.n_tiles * p.m_tiles * KB) // p.grid
-    return U, KB, max(1, min(p.grid, U // q))
+    return U, KB, max(1, min(p.grid, U // q)), 0
 
 
-def cta_of(u, U, G):
+def cta_of(u, U, G, KB, split):
+    if split:
+        t, kb = divmod(u, KB)
+        return t * split + ((kb + 1) * split + KB - 1) // KB - 1
     return ((u + 1) * G + U - 1) // U - 1
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (16, 4096, 12288)])
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (16, 4096, 12288), (64, 4096, 4096),
+                                   (128, 4096, 4096)])
 def test_withheld_partial_times_out_and_workspace_recovers(M, N, K):
     L = _lib.load()
     plan = nk.plan_for(M, N, K)
     assert plan.kind == nk.KIND_TC and plan.split_k == 0
-    U, KB, G = partition(plan.c, M)
-    assert G <= 148, "the grid must be one resident wave for the waiting protocol"
+    U, KB, G, split = partition(plan.c, M)
+    assert G <= 296, "the grid must be one resident wave for the waiting protocol"
     tile = 0
-    assert cta_of(KB - 1, U, G) > cta_of(0, U, G), "tile 0 must be shared by several CTAs"
+    assert cta_of(KB - 1, U, G, KB, split) > cta_of(0, U, G, KB, split), \
+        "tile 0 must be shared by several CTAs"
 
     W = synthetic.weight(N, K, seed=31, device=DEV)
     x = synthetic.activation(M, K, seed=32, device=DEV)
