@@ -670,7 +670,12 @@ def shape_rows(dev, cases, reps=5, chain=20, cublas=True, split=0):
         Ws = weights[(N, K)]
         x = synthetic.activation(M, K, seed=M, device=dev)
         y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-        plan = nk.plan_for(M, N, K, split_k=split)
+        if split < 0:
+            # the balanced persistent schedule alone: the plan without its tile-aligned slices
+            plan = nk.Plan(nk.m_bucket(M), N, K)
+            plan.c.slices = 0
+        else:
+            plan = nk.plan_for(M, N, K, split_k=split)
         row = {"model": model, "linear": name, "N": N, "K": K, "M": M}
         row.update(stats(timed(lambda W: nk.mm(x, W.t(), out=y, plan=plan, stream=stream)), M, N, K))
         if cublas:
@@ -696,7 +701,7 @@ def split_sweep(args):
     """--split-sweep: the Qwen3-8B decode linears (M 1..16; gate_up and lm_head at M 1 and 16)
     and the Qwen3-0.6B layer linears (M 1, 4, 8, 16) with split-K forced to every value 1..16
     beside the plan's own schedule (split 0: tile-aligned where the plan has slices, else
-    balanced), us per launch as in shape_rows."""
+    balanced) and the balanced schedule alone (split -1), us per launch as in shape_rows."""
     import neokernel_b200 as nk
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -708,12 +713,13 @@ def split_sweep(args):
     table, slices = {}, {}
     for _, name, N, K, M in cases:
         slices[f"{name} {N}x{K} M={M}"] = nk.plan_for(M, N, K).as_dict()["slices"]
-    for split in range(0, 17):
+    for split in range(-1, 17):
         for r in shape_rows(dev, cases, reps=3, cublas=False, split=split)["rows"]:
             table.setdefault(f"{r['model']} {r['linear']} M={r['M']}", {})[str(split)] = r["us"]
     print(json.dumps({"split_sweep_us": table, "plan_slices": slices,
                       "note": "split 0 = the plan's own schedule (tile-aligned with the plan's "
-                      "slices, else balanced persistent); 1..16 = one CTA per (tile, K slice)"}))
+                      "slices, else balanced persistent); -1 = the balanced schedule alone "
+                      "(slices cleared); 1..16 = one CTA per (tile, K slice)"}))
     return 0
 
 

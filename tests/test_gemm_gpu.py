@@ -249,6 +249,33 @@ def test_deterministic_across_runs():
             assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("N,K", [(6144, 4096), (4096, 4096), (4096, 12288), (1024, 2048)])
+@pytest.mark.parametrize("M", (1, 4, 8, 16))
+def test_tile_aligned_and_balanced_schedules(M, N, K):
+    """A plan with slices launches the tile-aligned schedule; the same plan with slices cleared
+    launches the balanced one. Interleaved on one workspace, each is within the tolerance of
+    the fp32 product, agrees with the sequential-fp32 oracle up to re-association, and gives
+    the same bits every time."""
+    W = weight_dev(N, K, seed=N + 5 * K)
+    x = synthetic.activation(M, K, seed=M + 11, device=DEV)
+    aligned = nk.plan_for(M, N, K)
+    assert aligned.as_dict()["slices"] >= 4
+    balanced = nk.Plan(nk.m_bucket(M), N, K)
+    balanced.c.slices = 0
+    ref = fp32_ref(x, W)
+    first = {}
+    for _ in range(2):
+        for name, plan in (("aligned", aligned), ("balanced", balanced)):
+            y = run(x, W, plan)
+            assert (y.float() - ref).abs().max().item() <= oracle.tolerance(K), name
+            if name in first:
+                assert torch.equal(y, first[name]), name
+            else:
+                first[name] = y
+                assert_vs_oracle(y, x, W)
+    assert nk.device_error() == 0
+
+
 def test_split_protocols_share_one_workspace():
     """Shared tiles are finished three ways: tagged partial slots (M <= 8), plain partials
     with a fence and a count (larger M), and, when a forced split makes the grid larger than
