@@ -39,8 +39,17 @@
 namespace nk {
 
 constexpr int kTcRows = kTcRowsPerCta;
-constexpr int kTcThreads = 192;            // 6 warps
-constexpr int kTcEpiThreads = 128;         // warps 2..5
+// Warps 0 and 1 load and issue; the epilogue has four warps (one per TMEM lane quarter), or
+// eight for token tiles of at least NK_TC_EPI8_MIN_NT, whose CTA is alone on its SM: then two
+// warps share each lane quarter and take alternate 16-column chunks. The epilogue's chunk
+// loops run latency-bound on one warp per scheduler (~2.5 k cycles a chunk measured on B200),
+// so the second warp halves the tail in which one CTA stores, publishes or sums a wide tile.
+#ifndef NK_TC_EPI8_MIN_NT
+#define NK_TC_EPI8_MIN_NT 64
+#endif
+__host__ __device__ constexpr int tc_epi_warps(int nt) { return nt >= NK_TC_EPI8_MIN_NT ? 8 : 4; }
+__host__ __device__ constexpr int tc_threads(int nt) { return 64 + 32 * tc_epi_warps(nt); }
+constexpr int kTcEpiThreads = 128;         // the four-warp epilogue
 constexpr uint32_t kWaitLimit = 1u << 26;  // polls before a wait gives up (seconds)
 
 // ---------------------------------------------------------------------------------------
@@ -193,8 +202,12 @@ __device__ __forceinline__ bool spin_until_count(const unsigned* count, unsigned
     return true;
 }
 
-__device__ __forceinline__ void epi_bar() {  // named barrier over the 4 epilogue warps
-    asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiThreads) : "memory");
+template <int THREADS>
+__device__ __forceinline__ void epi_bar_n() {  // named barrier over the epilogue warps
+    asm volatile("bar.sync 1, %0;" ::"n"(THREADS) : "memory");
+}
+__device__ __forceinline__ void epi_bar() {  // the four-warp epilogue's
+    epi_bar_n<kTcEpiThreads>();
 }
 
 // Shared-memory matrix descriptor for a K-major operand tile stored as 128-byte rows with
@@ -604,7 +617,8 @@ __device__ __forceinline__ void ar_publish(const GemmArgs& a, int set, int m, in
 }
 
 template <int NT, int MODE>
-__global__ void __launch_bounds__(kTcThreads) __maxnreg__(NT <= 64 ? NK_TC_MAXNREG : 255)
+__global__ void __launch_bounds__(tc_threads(NT))
+__maxnreg__(NT <= 64 ? NK_TC_MAXNREG : (tc_threads(NT) > 192 ? 200 : 255))
 tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
           GemmArgs a) {
     constexpr bool AMAX = MODE == kModeAmax;
@@ -649,7 +663,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar_tfull + 8 * i, 1);
-            mbar_init(bar_tempty + 8 * i, kTcEpiThreads / 32);
+            mbar_init(bar_tempty + 8 * i, tc_epi_warps(NT));
         }
         for (int i = 0; i < L::kPartBars; ++i) mbar_init(bar_part + 8 * i, 1);
         *abort_flag = 0u;
@@ -762,9 +776,13 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             }
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
+        // ---------------- epilogue (warps 2 and up) ----------------
         griddep_wait();
-        const int ep = threadIdx.x - 64;          // 0..127
+        constexpr int kEpiW = tc_epi_warps(NT);
+        constexpr int kEpiT = 32 * kEpiW;
+        constexpr int kHalves = kEpiW / 4;        // warps sharing one TMEM lane quarter
+        const int half = (warp - 2) >> 2;         // which of them this warp is
+        const int ep = threadIdx.x - 64;          // 0..kEpiT-1
         const int q = warp & 3;                   // TMEM lane quarter this warp may access
         const int row = 32 * q + lane;            // tile row owned by this thread
         const uint32_t tlane = (uint32_t)(32 * q) << 16;
@@ -811,7 +829,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             if constexpr (AR) {
                 if (whole || finisher) {
                     if (ep == 0) *ar_call = *ar_counter(a.ar_buf[a.ar_rank], sg.t) + 1u;
-                    epi_bar();
+                    epi_bar_n<kEpiT>();
                     ar_e = *ar_call;
                     ar_set = (int)(ar_e & 1u);
                 }
@@ -830,7 +848,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                 // loads (through L2) after that acquire
                 if (ep == 0)
                     *last_flag = spin_until_count(a.tickets + sg.t, (unsigned)(nseg - 1)) ? 1u : 0u;
-                epi_bar();
+                epi_bar_n<kEpiT>();
                 got = *last_flag != 0u;
             }
             if constexpr (NT == 16) {
@@ -864,7 +882,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                         qkv_rope_columns(a, qo, v, mcount, m0, sg.t, row, q, lane, ok, qk_smem);
                 } else if (ok) {
 #pragma unroll 1
-                    for (int c0 = 0; c0 < NT; c0 += 16) {
+                    for (int c0 = 16 * half; c0 < NT; c0 += 16 * kHalves) {
                         if (c0 >= mcount) break;  // warp-uniform
                         float v[16];
                         tmem_ld16(taddr + c0, v);
@@ -888,7 +906,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                 // by a fence and the tile's count.
                 if (ok && !withhold) {
 #pragma unroll 1
-                    for (int c0 = 0; c0 < NT; c0 += 16) {
+                    for (int c0 = 16 * half; c0 < NT; c0 += 16 * kHalves) {
                         if (c0 >= mcount) break;  // warp-uniform
                         float v[16];
                         tmem_ld16(taddr + c0, v);
@@ -911,7 +929,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                 int slots = partners >= 1 ? (int)(kRing / ((uint32_t)partners * kChunkBytes)) : 0;
                 slots = slots < L::kPartBars ? slots : L::kPartBars;
                 slots = slots < nchunks ? slots : nchunks;
-                const bool bulk = NT != 16 && !tagged && got && slots >= 1;
+                const bool bulk = NT != 16 && !tagged && got && slots >= kHalves;
                 if (ok && bulk) {
                     // Every MMA of this CTA is done, so the shared-memory ring is idle: pull each
                     // partner's partial columns [16k, 16k + 16) — contiguous fp32, [column][128
@@ -937,42 +955,47 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                         for (int k = 0; k < slots; ++k) issue(k);
                     }
 #pragma unroll 1
-                    for (int k = 0; k < nchunks; ++k) {
-                        const int h = k % slots;
-                        const bool arrived = __all_sync(
-                            0xffffffffu, mbar_wait(bar_part + 8 * h, (uint32_t)(k / slots) & 1u));
-                        float v[16];
-                        tmem_ld16(taddr + 16 * k, v);
-                        const float* sm =
-                            reinterpret_cast<const float*>(gbase + h * slot_bytes) + row;
-                        float ps[16];
+                    for (int r0 = 0; r0 < nchunks; r0 += kHalves) {
+                        const int k = r0 + half;  // this warp's chunk of the round
+                        if (k < nchunks) {
+                            const int h = k % slots;
+                            const bool arrived = __all_sync(
+                                0xffffffffu, mbar_wait(bar_part + 8 * h, (uint32_t)(k / slots) & 1u));
+                            float v[16];
+                            tmem_ld16(taddr + 16 * k, v);
+                            const float* sm =
+                                reinterpret_cast<const float*>(gbase + h * slot_bytes) + row;
+                            float ps[16];
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) ps[j] = 0.f;
-                        for (int i = 0; i < partners; ++i)
+                            for (int j = 0; j < 16; ++j) ps[j] = 0.f;
+                            for (int i = 0; i < partners; ++i)
 #pragma unroll
-                            for (int j = 0; j < 16; ++j) ps[j] += sm[(i * 16 + j) * kTcRows];
+                                for (int j = 0; j < 16; ++j) ps[j] += sm[(i * 16 + j) * kTcRows];
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] += ps[j];
-                        if constexpr (AR) {
-                            if (arrived && n < a.N)
+                            for (int j = 0; j < 16; ++j) v[j] += ps[j];
+                            if constexpr (AR) {
+                                if (arrived && n < a.N)
+#pragma unroll
+                                    for (int j = 0; j < 16; ++j)
+                                        if (16 * k + j < mcount)
+                                            ar_publish(a, ar_set, m0 + 16 * k + j, n, v[j]);
+                            } else if (store_y && arrived && n < a.N) {
 #pragma unroll
                                 for (int j = 0; j < 16; ++j)
                                     if (16 * k + j < mcount)
-                                        ar_publish(a, ar_set, m0 + 16 * k + j, n, v[j]);
-                        } else if (store_y && arrived && n < a.N) {
-#pragma unroll
-                            for (int j = 0; j < 16; ++j)
-                                if (16 * k + j < mcount)
-                                    store_out(a, (int64_t)(m0 + 16 * k + j) * a.ldy + n, v[j]);
+                                        store_out(a, (int64_t)(m0 + 16 * k + j) * a.ldy + n, v[j]);
+                            }
+                            if constexpr (AMAX)
+                                amax_fold16(a, arrived && n < a.N, n, m0 + 16 * k,
+                                            min(16, mcount - 16 * k), v);
                         }
-                        if constexpr (AMAX)
-                            amax_fold16(a, arrived && n < a.N, n, m0 + 16 * k,
-                                        min(16, mcount - 16 * k), v);
-                        if (k + slots < nchunks) {
-                            epi_bar();  // every thread is done with this slot
+                        // every chunk of the round is done with its slot: refill those slots
+                        if (r0 + slots < nchunks) {
+                            epi_bar_n<kEpiT>();
                             if (ep == 0) {
                                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                                issue(k + slots);
+                                for (int kk = r0; kk < r0 + kHalves && kk + slots < nchunks; ++kk)
+                                    issue(kk + slots);
                             }
                         }
                     }
@@ -989,7 +1012,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                                   reinterpret_cast<float*>(gbase));
                 } else if (ok) {
 #pragma unroll 1
-                    for (int c0 = 0; c0 < NT; c0 += 16) {
+                    for (int c0 = 16 * half; c0 < NT; c0 += 16 * kHalves) {
                         if (c0 >= mcount) break;  // warp-uniform
                         if constexpr (NT != 16) {
 #pragma unroll
@@ -1024,23 +1047,23 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             if (lane == 0) mbar_arrive(bar_tempty + 8 * buf);
             if (!whole && wait_mode && !tagged && rank > 0) {
                 // this CTA's partial stores (ordered before the barrier), then one release
-                epi_bar();
+                epi_bar_n<kEpiT>();
                 if (ep == 0 && !withhold) count_release(a.tickets + sg.t);
             } else if (!whole && !wait_mode) {
                 // Without a co-resident grid every rank publishes plain partials (rank 0 above as
                 // well) and the CTA whose arrival completes the tile's count sums them, in the
                 // same order as the waiting scheme: rank 0 + (rank 1 + rank 2 + ...).
                 __threadfence();
-                epi_bar();
+                epi_bar_n<kEpiT>();
                 if (ep == 0) {
                     const unsigned prev = atomicAdd(a.tickets + sg.t, 1u);
                     *last_flag = (prev == (unsigned)(nseg - 1)) ? 1u : 0u;
                 }
-                epi_bar();
+                epi_bar_n<kEpiT>();
                 if (*last_flag) {
                     __threadfence();
                     const bool live = n < a.N && *abort_flag == 0u;
-                    for (int c0 = 0; c0 < mcount; c0 += 16) {
+                    for (int c0 = 16 * half; c0 < mcount; c0 += 16 * kHalves) {
                         float ps[16];
 #pragma unroll
                         for (int j = 0; j < 16; ++j) ps[j] = 0.f;
@@ -1059,7 +1082,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                     }
                     if (ep == 0) a.tickets[sg.t] = 0u;  // re-armed for the next launch
                 }
-                epi_bar();  // last_flag is rewritten by the next partial segment
+                epi_bar_n<kEpiT>();  // last_flag is rewritten by the next partial segment
             }
             if constexpr (AR) {
                 if (whole || finisher) {
@@ -1069,7 +1092,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                     uint8_t* own = a.ar_buf[a.ar_rank];
                     __threadfence_system();  // this thread's slot stores, before the flags
                     if (ep == 0) *ar_ok = 1u;
-                    epi_bar();
+                    epi_bar_n<kEpiT>();
                     if (ep < a.ar_world)
                         st_release_sys(ar_flag(a.ar_buf[ep], ar_set, a.ar_rank, sg.t), ar_e);
                     if (ep < a.ar_world) {
@@ -1084,9 +1107,9 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
                             __nanosleep(64);
                         }
                     }
-                    epi_bar();
+                    epi_bar_n<kEpiT>();
                     if (*ar_ok && n < a.N) {
-                        for (int j = 0; j < mcount; ++j) {
+                        for (int j = half; j < mcount; j += kHalves) {
                             const size_t off = (size_t)(m0 + j) * a.N + n;
                             float acc =
                                 __ldcg(ar_slot(own, ar_set, 0, a.ar_world, a.ar_max_elems) + off);
@@ -1103,12 +1126,12 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
             // The CTA whose arrival completes the count turns the keys into indices and
             // leaves keys and count zero for the next call.
             __threadfence();  // this thread's key updates, before the CTA's arrival
-            epi_bar();
+            epi_bar_n<kEpiT>();
             if (ep == 0) *last_flag = atomicAdd(a.amax_done, 1u) == gridDim.x - 1 ? 1u : 0u;
-            epi_bar();
+            epi_bar_n<kEpiT>();
             if (*last_flag) {
                 __threadfence();
-                for (int m = ep; m < a.M; m += kTcEpiThreads) {
+                for (int m = ep; m < a.M; m += kEpiT) {
                     const unsigned long long k =
                         atomicExch(a.amax_keys + (size_t)m * (kAmaxKeyStride / 8), 0ull);
                     a.amax_idx[m] = k ? (int64_t)(0xFFFFFFFFu - (uint32_t)k) : (int64_t)-1;
@@ -1222,13 +1245,13 @@ static int tc_resident_per_sm(int dev) {
         cudaDeviceGetAttribute(&thr_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev) !=
             cudaSuccess)
         return 0;
-    constexpr int kWarps = kTcThreads / 32;
+    constexpr int kWarps = tc_threads(NT) / 32;
     // registers: 8-register steps per thread, and each of the 4 sub-partitions holds its
     // quarter of the register file for at most ceil(warps / 4) warps of every CTA
     const int regs_warp = ((fa.numRegs + 7) & ~7) * 32;
     const int by_regs = (regs_sm / 4) / (regs_warp * ((kWarps + 3) / 4));
     const int by_smem = smem_sm / (L::kAlloc + (int)fa.sharedSizeBytes + reserved);
-    const int by_thr = thr_sm / kTcThreads;
+    const int by_thr = thr_sm / tc_threads(NT);
     const int by_tmem = 512 / L::kTmemCols;
     int n = L::kPerSm;
     for (int lim : {by_regs, by_smem, by_thr, by_tmem}) n = lim < n ? lim : n;
@@ -1290,7 +1313,7 @@ static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
     const int grid = P.G;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
-    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.blockDim = dim3(tc_threads(NT), 1, 1);
     cfg.dynamicSmemBytes = L::kAlloc;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
