@@ -39,16 +39,36 @@
 namespace nk {
 
 constexpr int kTcRows = kTcRowsPerCta;
-// Warps 0 and 1 load and issue; the epilogue has four warps (one per TMEM lane quarter), or
-// eight for token tiles of at least NK_TC_EPI8_MIN_NT, whose CTA is alone on its SM: then two
-// warps share each lane quarter and take alternate 16-column chunks. The epilogue's chunk
-// loops run latency-bound on one warp per scheduler (~2.5 k cycles a chunk measured on B200),
-// so the second warp halves the tail in which one CTA stores, publishes or sums a wide tile.
-#ifndef NK_TC_EPI8_MIN_NT
-#define NK_TC_EPI8_MIN_NT 64
+// Warps 0 and 1 load and issue; the epilogue has four warps (one per TMEM lane quarter) for
+// the decode token tiles, eight for the 64-token tile and twelve for wider ones, whose CTA is
+// alone on its SM: two or three warps then share each lane quarter and take 16-column chunks
+// in turn. The epilogue's chunk loops run latency-bound on one warp per scheduler (~2.5 k
+// cycles a chunk measured on B200), so every added warp shortens the tail in which one CTA
+// stores, publishes or sums a wide tile. Measured (verify M = 64 / 128 / 256, µs, four ->
+// eight -> twelve warps): o_proj 16.9 -> 14.0 -> 14.1, 25.4 -> 19.6 -> 18.3, 27.6 -> 21.8 ->
+// 20.5; sixteen warps would leave 96 registers a thread and spill.
+#ifndef NK_TC_EPI_WARPS_64
+#define NK_TC_EPI_WARPS_64 8
 #endif
-__host__ __device__ constexpr int tc_epi_warps(int nt) { return nt >= NK_TC_EPI8_MIN_NT ? 8 : 4; }
+#ifndef NK_TC_EPI_WARPS_128
+#define NK_TC_EPI_WARPS_128 12
+#endif
+__host__ __device__ constexpr int tc_epi_warps(int nt) {
+    return nt >= 128 ? NK_TC_EPI_WARPS_128 : (nt >= 64 ? NK_TC_EPI_WARPS_64 : 4);
+}
 __host__ __device__ constexpr int tc_threads(int nt) { return 64 + 32 * tc_epi_warps(nt); }
+// Registers a thread may use. Every CTA of the grid must be resident at once (rank-0 CTAs of
+// shared tiles wait for higher CTAs), and the launch caps the grid by the CTAs that fit per
+// SM: two CTAs of six warps per SM need at most 128 registers a thread (each SM sub-partition
+// holds up to four of the twelve warps), the cap for token tiles <= 64; a wide tile's CTA,
+// alone on its SM, may use a sub-partition's 16K registers over the warps it places there
+// (ceil(warps / 4)), at most 255.
+__host__ __device__ constexpr int tc_reg_budget(int nt) {
+    return (16384 / (((tc_threads(nt) / 32 + 3) / 4) * 32)) & ~7;
+}
+__host__ __device__ constexpr int tc_maxnreg(int nt) {
+    return (nt <= 64 ? 128 : 255) < tc_reg_budget(nt) ? (nt <= 64 ? 128 : 255) : tc_reg_budget(nt);
+}
 constexpr int kTcEpiThreads = 128;         // the four-warp epilogue
 constexpr uint32_t kWaitLimit = 1u << 26;  // polls before a wait gives up (seconds)
 
@@ -450,11 +470,6 @@ __device__ __forceinline__ Segment segment_at(int64_t u, int64_t u_end, int KB) 
     return sg;
 }
 
-// Every CTA of the grid must be resident at once (rank-0 CTAs of shared tiles wait for
-// higher CTAs), and the launch caps the grid by the CTAs that fit per SM. Two CTAs of six
-// warps per SM need at most 128 registers a thread (each SM sub-partition holds up to four
-// of the twelve warps), hence the cap for the token tiles that fit twice in shared memory.
-#define NK_TC_MAXNREG 128
 // Kernel variants (template MODE), each compiled only with its own code:
 //   kModePlain: y = x · Wᵀ (nk_gemm_bf16, nk_gemm_bf16_f32out, nk_gemm_bf16_static);
 //   kModeAmax:  the greedy head (nk_gemm_bf16_argmax) — folds every final output into the
@@ -617,14 +632,15 @@ __device__ __forceinline__ void ar_publish(const GemmArgs& a, int set, int m, in
 }
 
 template <int NT, int MODE>
-__global__ void __launch_bounds__(tc_threads(NT))
-__maxnreg__(NT <= 64 ? NK_TC_MAXNREG : (tc_threads(NT) > 192 ? 200 : 255))
+__global__ void __launch_bounds__(tc_threads(NT)) __maxnreg__(tc_maxnreg(NT))
 tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
           GemmArgs a) {
     constexpr bool AMAX = MODE == kModeAmax;
     constexpr bool AR = MODE == kModeAr;
     constexpr bool QKV = MODE == kModeQkv;
     static_assert(!QKV || NT == 16, "the fused QKV epilogue takes decode token tiles");
+    static_assert(((tc_threads(NT) / 32 + 3) / 4) * 32 * tc_maxnreg(NT) <= 16384,
+                  "one CTA's warps must fit a sub-partition's register file");
     constexpr int kTcUK = tc_uk(NT);       // boxes along K per stage
     constexpr int kTcKStep = tc_kstep(NT);  // K elements per unit
     using L = TcSmem<NT, QKV ? kQkvSmemBytes : 0>;
