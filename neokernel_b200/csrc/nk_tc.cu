@@ -797,7 +797,9 @@ tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CU
         constexpr int kEpiW = tc_epi_warps(NT);
         constexpr int kEpiT = 32 * kEpiW;
         constexpr int kHalves = kEpiW / 4;        // warps sharing one TMEM lane quarter
-        const int half = (warp - 2) >> 2;         // which of them this warp is
+        // which of them this warp is (a constant 0 with one warp per quarter, so that the
+        // decode token tile's single-chunk loops fold as before)
+        const int half = kHalves > 1 ? (warp - 2) >> 2 : 0;
         const int ep = threadIdx.x - 64;          // 0..kEpiT-1
         const int q = warp & 3;                   // TMEM lane quarter this warp may access
         const int row = 32 * q + lane;            // tile row owned by this thread
