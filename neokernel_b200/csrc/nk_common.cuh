@@ -212,18 +212,30 @@ struct TcPartition {
     int KB;      // units (K blocks) per tile
     int G;       // CTAs
     int split;   // 0 = balanced
+    int lead;    // split > 1: rank 0's slice is KB / split + lead units, the others share the
+                 // rest evenly (0 = every slice KB / split)
 
+    __host__ __device__ int lead_units() const {
+        const int a = KB / split + lead;
+        return a < KB - (split - 1) ? a : KB - (split - 1);
+    }
     __host__ __device__ int64_t begin(int c) const {
         if (split == 0) return (U * (int64_t)c) / G;
         const int t = c / split, s = c % split;
-        return (int64_t)t * KB + ((int64_t)s * KB) / split;
+        if (lead == 0 || split < 2 || s == 0) return (int64_t)t * KB + ((int64_t)s * KB) / split;
+        const int A = lead_units();
+        return (int64_t)t * KB + A + ((int64_t)(s - 1) * (KB - A)) / (split - 1);
     }
     // The CTA whose range contains unit u.
     __host__ __device__ int cta_of(int64_t u) const {
         if (split == 0) return (int)(((u + 1) * G + U - 1) / U - 1);
         const int64_t t = u / KB;
         const int64_t kb = u - t * KB;
-        return (int)(t * split + ((kb + 1) * split + KB - 1) / KB - 1);
+        if (lead == 0 || split < 2) return (int)(t * split + ((kb + 1) * split + KB - 1) / KB - 1);
+        const int A = lead_units();
+        if (kb < A) return (int)(t * split);
+        const int64_t v = kb - A, R = KB - A;
+        return (int)(t * split + 1 + ((v + 1) * (split - 1) + R - 1) / R - 1);
     }
     __host__ __device__ int first_cta(int t) const { return cta_of((int64_t)t * KB); }
     __host__ __device__ int last_cta(int t) const { return cta_of((int64_t)(t + 1) * KB - 1); }
@@ -345,6 +357,17 @@ __host__ __device__ constexpr int tc_kstep(int nt) { return kTcBox * tc_uk(nt); 
 #endif
 #ifndef NK_TC_MIN_SLICES
 #define NK_TC_MIN_SLICES 4
+#endif
+// Extra K blocks for the tile-aligned schedule's rank-0 slice (see tc_lead in nk_tc.cu): for
+// tiles of at least 32 K blocks, by finishing protocol; the counted protocol's for 16..31.
+#ifndef NK_TC_LEAD_TAGGED
+#define NK_TC_LEAD_TAGGED 2
+#endif
+#ifndef NK_TC_LEAD_COUNTED
+#define NK_TC_LEAD_COUNTED 4
+#endif
+#ifndef NK_TC_LEAD_COUNTED_SHORT
+#define NK_TC_LEAD_COUNTED_SHORT 3
 #endif
 constexpr int kGenericRows = 8;          // rows per CTA in the generic kernel
 constexpr int kGenericTokens = 8;        // tokens per CTA in the generic kernel

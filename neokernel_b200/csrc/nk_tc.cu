@@ -1276,6 +1276,20 @@ static int tc_resident_per_sm(int dev) {
     return n;
 }
 
+// K blocks added to the rank-0 slice of each tile in the tile-aligned schedule. All of a
+// tile's CTAs stream equal slices, so they finish together and the partners' publishing, the
+// count and rank 0's poll (~2 us at M = 16) all follow the streaming; a longer rank-0 slice
+// (taken evenly from the partners) hides them behind rank 0's own streaming. Measured on B200,
+// 20 chained launches, us (no lead -> this lead): Qwen3-8B QKV M=1 9.54 -> 9.27, M=8
+// 11.13 -> 10.39, M=16 12.39 -> 11.46; o_proj M=8 9.55 -> 9.23; down M=16 20.09 -> 19.73;
+// Qwen3-0.6B down M=16 8.14 -> 7.54. Tiles of fewer than 16 K blocks (0.6B QKV) lost with
+// any lead, and short tiles lost it under the tagged protocol.
+static int tc_lead(int KB, bool tagged) {
+    if (KB >= 32) return tagged ? NK_TC_LEAD_TAGGED : NK_TC_LEAD_COUNTED;
+    if (KB >= 16) return tagged ? 0 : NK_TC_LEAD_COUNTED_SHORT;
+    return 0;
+}
+
 template <int NT, int MODE>
 static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
                        const CUtensorMap& mx, cudaStream_t s) {
@@ -1307,6 +1321,9 @@ static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
         // takes it, so that the fused forms add the same partials in the same order as the
         // plain launches they replace)
         P.split = p.slices;
+        const bool tagged = a.M <= NK_TC_TAG_MAX_M &&
+                            a.M * (p.slices - 1) <= 4 * NK_TC_TAG_MAX_M;  // as the epilogue decides
+        P.lead = tc_lead(P.KB, tagged);
         P.G = (int)(tiles * p.slices);
         a.seg_max = p.slices;
     } else {
@@ -1356,6 +1373,7 @@ int launch_tc(const nk_plan& p, const GemmArgs& in, cudaStream_t s) {
     P.KB = KB;
     P.U = (int64_t)p.n_tiles * m_tiles * KB;
     P.split = p.split_k;
+    P.lead = 0;
     P.G = 1;  // set by launch_tc_t once the device's residency is known
     CUtensorMap mw, mx;
     if (make_map(&mw, a.w, a.N, a.K, a.ldw, kTcRows) != NK_OK) return NK_ERR_ALIGN;

@@ -99,32 +99,45 @@ def test_forced_split_with_too_many_tiles_is_refused():
 class Partition:
     """Python mirror of TcPartition (neokernel_b200/csrc/nk_common.cuh)."""
 
-    def __init__(self, U, KB, G, split):
-        self.U, self.KB, self.G, self.split = U, KB, G, split
+    def __init__(self, U, KB, G, split, lead=0):
+        self.U, self.KB, self.G, self.split, self.lead = U, KB, G, split, lead
+
+    def lead_units(self):
+        return min(self.KB // self.split + self.lead, self.KB - (self.split - 1))
 
     def begin(self, c):
         if self.split == 0:
             return (self.U * c) // self.G
         t, s = divmod(c, self.split)
-        return t * self.KB + (s * self.KB) // self.split
+        if self.lead == 0 or self.split < 2 or s == 0:
+            return t * self.KB + (s * self.KB) // self.split
+        A = self.lead_units()
+        return t * self.KB + A + ((s - 1) * (self.KB - A)) // (self.split - 1)
 
     def cta_of(self, u):
         if self.split == 0:
             return ((u + 1) * self.G + self.U - 1) // self.U - 1
         t, kb = divmod(u, self.KB)
-        return t * self.split + ((kb + 1) * self.split + self.KB - 1) // self.KB - 1
+        if self.lead == 0 or self.split < 2:
+            return t * self.split + ((kb + 1) * self.split + self.KB - 1) // self.KB - 1
+        A = self.lead_units()
+        if kb < A:
+            return t * self.split
+        v, R = kb - A, self.KB - A
+        return t * self.split + 1 + ((v + 1) * (self.split - 1) + R - 1) // R - 1
 
 
-def launch_partition(p, M, aligned=False):
+def launch_partition(p, M, aligned=False, lead=0):
     """The partition launch_tc (nk_tc.cu) builds for a call with M tokens: the tile-aligned
-    one (a plan with slices, whole grid resident) or the balanced one."""
+    one (a plan with slices, whole grid resident; its rank-0 slice `lead` K blocks longer) or
+    the balanced one."""
     KB = -(-p.K // p.k_step)
     m_tiles = -(-M // p.tile_m)
     U = p.n_tiles * m_tiles * KB
     if p.split_k:
         return Partition(U, KB, p.n_tiles * m_tiles * p.split_k, p.split_k)
     if aligned:
-        return Partition(U, KB, p.n_tiles * m_tiles * p.slices, p.slices)
+        return Partition(U, KB, p.n_tiles * m_tiles * p.slices, p.slices, lead)
     q = (p.n_tiles * p.m_tiles * KB) // p.grid
     G = max(1, min(p.grid, U // q))
     return Partition(U, KB, G, 0)
@@ -136,11 +149,12 @@ def check_tc_partition(p, M_max):
     if not p.split_k:
         assert p.grid <= 148 * 2
         assert p.slices == 0 or p.n_tiles * p.m_tiles * p.slices <= 148 * 2
-    schedules = [(M, False) for M in sorted({1, M_max, max(1, M_max // 2)})]
+    schedules = [(M, False, 0) for M in sorted({1, M_max, max(1, M_max // 2)})]
     if p.slices:
-        schedules += [(M, True) for M in sorted({1, M_max})]
-    for M, aligned in schedules:
-        P = launch_partition(p, M, aligned)
+        # every rank-0 lead the kernel may be built with (nk_common.cuh, NK_TC_LEAD_*)
+        schedules += [(M, True, lead) for M in sorted({1, M_max}) for lead in range(0, 9)]
+    for M, aligned, lead in schedules:
+        P = launch_partition(p, M, aligned, lead)
         assert P.begin(0) == 0 and P.begin(P.G) == P.U
         cover = []
         for c in range(P.G):
