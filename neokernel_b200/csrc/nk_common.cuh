@@ -366,6 +366,9 @@ __host__ __device__ constexpr int tc_kstep(int nt) { return kTcBox * tc_uk(nt); 
 #ifndef NK_TC_LEAD_COUNTED
 #define NK_TC_LEAD_COUNTED 4
 #endif
+#ifndef NK_TC_LEAD_COUNTED_WIDE  // counted, tiles of >= 32 K blocks split 7 or more ways
+#define NK_TC_LEAD_COUNTED_WIDE 6
+#endif
 #ifndef NK_TC_LEAD_COUNTED_SHORT
 #define NK_TC_LEAD_COUNTED_SHORT 3
 #endif

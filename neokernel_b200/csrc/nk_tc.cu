@@ -1281,11 +1281,14 @@ static int tc_resident_per_sm(int dev) {
 // count and rank 0's poll (~2 us at M = 16) all follow the streaming; a longer rank-0 slice
 // (taken evenly from the partners) hides them behind rank 0's own streaming. Measured on B200,
 // 20 chained launches, us (no lead -> this lead): Qwen3-8B QKV M=1 9.54 -> 9.27, M=8
-// 11.13 -> 10.39, M=16 12.39 -> 11.46; o_proj M=8 9.55 -> 9.23; down M=16 20.09 -> 19.73;
-// Qwen3-0.6B down M=16 8.14 -> 7.54. Tiles of fewer than 16 K blocks (0.6B QKV) lost with
-// any lead, and short tiles lost it under the tagged protocol.
-static int tc_lead(int KB, bool tagged) {
-    if (KB >= 32) return tagged ? NK_TC_LEAD_TAGGED : NK_TC_LEAD_COUNTED;
+// 11.13 -> 10.39, M=16 12.39 -> 11.46; o_proj M=8 9.55 -> 9.14, M=16 10.27 -> 9.73; down
+// M=16 20.09 -> 19.83; Qwen3-0.6B down M=16 8.14 -> 7.54. Tiles split 7 or more ways (o_proj,
+// down) take a longer lead than QKV's 6-way tiles, which lost with it; tiles of fewer than 16
+// K blocks (0.6B QKV) lost with any lead, and short tiles lost it under the tagged protocol.
+static int tc_lead(int KB, int slices, bool tagged) {
+    if (KB >= 32)
+        return tagged ? NK_TC_LEAD_TAGGED
+                      : (slices >= 7 ? NK_TC_LEAD_COUNTED_WIDE : NK_TC_LEAD_COUNTED);
     if (KB >= 16) return tagged ? 0 : NK_TC_LEAD_COUNTED_SHORT;
     return 0;
 }
@@ -1323,7 +1326,7 @@ static int launch_tc_t(const nk_plan& p, GemmArgs& a, const CUtensorMap& mw,
         P.split = p.slices;
         const bool tagged = a.M <= NK_TC_TAG_MAX_M &&
                             a.M * (p.slices - 1) <= 4 * NK_TC_TAG_MAX_M;  // as the epilogue decides
-        P.lead = tc_lead(P.KB, tagged);
+        P.lead = tc_lead(P.KB, p.slices, tagged);
         P.G = (int)(tiles * p.slices);
         a.seg_max = p.slices;
     } else {
